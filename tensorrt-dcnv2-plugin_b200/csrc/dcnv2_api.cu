@@ -1,0 +1,409 @@
+// dcnv2_api.cu — host side of libdcnv2.so: validation, the launch plan (tile shape, pipeline
+// depth, TMEM columns, workspace layout) and the stateless C ABI declared in include/dcnv2.h.
+//
+// Replaces the dispatch in DCNv2Plugin::enqueue (src/dcn_plugin.cpp:122-176) and the workspace
+// rule of getWorkspaceSize (:110-118). Differences from the reference, all deliberate:
+//   * every image of the batch is computed (the reference reads only image 0, :125-130);
+//   * deformable_groups is honoured (the reference stores it but never uses it, :197);
+//   * the workspace holds a channels-last copy of x and the packed weights instead of the
+//     fp32 column matrix, and it scales with N;
+//   * failures are reported as dcnv2_status values (the reference returns 0 unconditionally).
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/dcnv2.h"
+#include "../../include/dcnv2_diag.h"
+#include "dcnv2_kernels.cuh"
+
+namespace dcnv2 {
+
+namespace {
+
+constexpr size_t kSmemLimit = 227 * 1024;     // opt-in dynamic shared memory per block
+constexpr size_t kErrBytes = 256;
+constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;  // 2 s per on-chip wait
+
+struct DevInfo {
+  int sm_count = 0;
+  int major = 0;
+  int minor = 0;
+  bool ok = false;
+  std::atomic<uint32_t> attr_set{0};
+};
+constexpr int kMaxDevices = 64;
+DevInfo g_dev[kMaxDevices];
+std::once_flag g_dev_once[kMaxDevices];
+
+DevInfo* device_info(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::call_once(g_dev_once[dev], [dev]() {
+    DevInfo& d = g_dev[dev];
+    if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+      cudaGetLastError();
+      d.ok = false;
+      return;
+    }
+    d.ok = true;
+  });
+  return &g_dev[dev];
+}
+
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct Plan {
+  int prec = 0;
+  bool fused = false;
+  int N, C, H, W, O, K, T, stride, pad, dil, dg, Ho, Wo, P, Cg;
+  int elem_bytes;
+  // fused-kernel configuration
+  int CBg = 0, numKB = 0, cchunks = 0, nrows = 0, nsub = 0, n_mma = 0, acc_bufs = 0;
+  int stages = 0, tiles_per_img = 0, num_tiles = 0;
+  uint32_t tmem_cols = 0, a_stage_bytes = 0, b_stage_bytes = 0;
+  size_t smem_bytes = 0;
+  // workspace layout (offsets from the 256-byte aligned base)
+  size_t off_x = 0, off_w = 0, ws_bytes = 0;
+  bool tf32_single = false, precise = false;
+};
+
+int prec_of(int dtype) {
+  switch (dtype) {
+    case DCNV2_FLOAT: return PREC_F32;
+    case DCNV2_HALF: return PREC_F16;
+    case DCNV2_INT8: return PREC_I8;
+    default: return -1;
+  }
+}
+
+int elem_bytes_of(int prec) { return prec == PREC_F32 ? 4 : prec == PREC_F16 ? 2 : 1; }
+int chunk_elems_of(int prec) { return prec == PREC_F32 ? 4 : prec == PREC_F16 ? 8 : 16; }
+int block_elems_of(int prec) { return prec == PREC_F32 ? 32 : prec == PREC_F16 ? 64 : 128; }
+
+dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
+  if (!d || !pl) return DCNV2_ERR_INVALID_ARG;
+  if (d->n < 1 || d->c < 1 || d->h < 1 || d->w < 1 || d->out_c < 1 || d->kernel < 1 ||
+      d->stride < 1 || d->padding < 0 || d->dilation < 1 || d->deformable_groups < 1)
+    return DCNV2_ERR_INVALID_ARG;
+  if (d->c % d->deformable_groups) return DCNV2_ERR_INVALID_ARG;
+  if (d->math < DCNV2_MATH_DEFAULT || d->math > DCNV2_MATH_SIMT) return DCNV2_ERR_INVALID_ARG;
+  const int prec = prec_of(d->dtype);
+  if (prec < 0) return DCNV2_ERR_UNSUPPORTED;
+  if (d->math == DCNV2_MATH_TF32 && prec != PREC_F32) return DCNV2_ERR_INVALID_ARG;
+  const int64_t ho = (int64_t(d->h) + 2 * int64_t(d->padding) -
+                      int64_t(d->dilation) * (d->kernel - 1) - 1);
+  const int64_t wo = (int64_t(d->w) + 2 * int64_t(d->padding) -
+                      int64_t(d->dilation) * (d->kernel - 1) - 1);
+  if (ho < 0 || wo < 0) return DCNV2_ERR_INVALID_ARG;
+  Plan& p = *pl;
+  p.prec = prec;
+  p.N = d->n; p.C = d->c; p.H = d->h; p.W = d->w; p.O = d->out_c; p.K = d->kernel;
+  p.T = d->kernel * d->kernel; p.stride = d->stride; p.pad = d->padding; p.dil = d->dilation;
+  p.dg = d->deformable_groups; p.Cg = d->c / d->deformable_groups;
+  p.Ho = static_cast<int>(ho / d->stride + 1);
+  p.Wo = static_cast<int>(wo / d->stride + 1);
+  p.elem_bytes = elem_bytes_of(prec);
+  const int64_t P = int64_t(p.Ho) * p.Wo;
+  const int64_t plane = int64_t(p.H) * p.W * p.C;
+  // 32-bit index limits inside one image (the batch index is 64-bit everywhere).
+  if (P >= (int64_t(1) << 31) || plane >= (int64_t(1) << 31) ||
+      int64_t(p.O) * P >= (int64_t(1) << 31) || int64_t(p.T) * p.dg * 2 >= (int64_t(1) << 31) ||
+      int64_t(p.O) * p.C * p.T >= (int64_t(1) << 31))
+    return DCNV2_ERR_INVALID_ARG;
+  p.P = static_cast<int>(P);
+  p.tf32_single = (d->math == DCNV2_MATH_TF32);
+  p.precise = (d->math == DCNV2_MATH_PRECISE);
+
+  p.fused = (d->math != DCNV2_MATH_SIMT) && (p.Cg % chunk_elems_of(prec) == 0);
+  if (p.fused) {
+    const int KC = block_elems_of(prec);
+    const int nA = prec == PREC_F32 ? 2 : 1, nB = nA;
+    p.CBg = static_cast<int>(cdiv(p.Cg, KC));
+    const int64_t numKB = int64_t(p.dg) * p.T * p.CBg;
+    const int max_rows = prec == PREC_F32 ? 256 : 512;
+    p.cchunks = static_cast<int>(cdiv(p.O, max_rows));
+    const int rows_per_chunk = static_cast<int>(cdiv(p.O, p.cchunks));
+    p.nsub = static_cast<int>(cdiv(rows_per_chunk, 256));
+    p.n_mma = static_cast<int>(cdiv(cdiv(rows_per_chunk, p.nsub), 16) * 16);
+    p.nrows = p.nsub * p.n_mma;
+    p.acc_bufs = (2 * p.nrows <= 512) ? 2 : 1;
+    uint32_t cols = 32;
+    while (cols < static_cast<uint32_t>(p.acc_bufs * p.nrows)) cols <<= 1;
+    p.tmem_cols = cols;
+    p.a_stage_bytes = static_cast<uint32_t>(nA * kATileBytes);
+    p.b_stage_bytes = static_cast<uint32_t>(nB * p.nrows * kRowBytes);
+    const size_t per_stage = p.a_stage_bytes + p.b_stage_bytes;
+    const size_t fixed = 1024 + 512;  // alignment slack + barriers and flags
+    int stages = static_cast<int>((kSmemLimit - fixed) / per_stage);
+    if (stages > kMaxStages) stages = kMaxStages;
+    const int64_t tiles_per_img = cdiv(P, kTileM);
+    const int64_t num_tiles = int64_t(p.N) * tiles_per_img * p.cchunks;
+    if (stages < 2 || numKB >= (int64_t(1) << 31) || num_tiles >= (int64_t(1) << 31)) {
+      p.fused = false;
+    } else {
+      p.stages = stages;
+      p.numKB = static_cast<int>(numKB);
+      p.tiles_per_img = static_cast<int>(tiles_per_img);
+      p.num_tiles = static_cast<int>(num_tiles);
+      p.smem_bytes = fixed + size_t(stages) * per_stage;
+    }
+  }
+  // Workspace: [error word | x channels-last | packed weights]; +256 so that any base pointer
+  // can be aligned up to 256 bytes.
+  size_t off = kErrBytes;
+  if (p.fused) {
+    p.off_x = off;
+    off = align_up(off + size_t(p.N) * plane * p.elem_bytes, 1024);
+    p.off_w = off;
+    off += size_t(p.cchunks) * p.numKB * p.b_stage_bytes;
+  }
+  p.ws_bytes = align_up(off, 256) + 256;
+  return DCNV2_OK;
+}
+
+template <int PREC>
+dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, const void* offset,
+                          const void* mask, const void* weight, const void* bias, void* y,
+                          uint8_t* ws, float scale, cudaStream_t st) {
+  using TR = PrecTraits<PREC>;
+  using XT = typename TR::X;
+  const uint32_t bit = 1u << PREC;
+  if (!(di->attr_set.load(std::memory_order_acquire) & bit)) {
+    if (cudaFuncSetAttribute(dcnv2_fused_kernel<PREC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemLimit)) != cudaSuccess)
+      return DCNV2_ERR_CUDA;
+    di->attr_set.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  (void)dev;
+  int* err = reinterpret_cast<int*>(ws);
+  XT* x_nhwc = reinterpret_cast<XT*>(ws + p.off_x);
+  uint8_t* wpack = ws + p.off_w;
+
+  // 1) x: NCHW -> NHWC
+  {
+    constexpr int TILE = 32 * (4 / sizeof(XT));
+    const int HW = p.H * p.W;
+    dim3 grid(static_cast<unsigned>(cdiv(HW, TILE)), static_cast<unsigned>(cdiv(p.C, TILE)),
+              static_cast<unsigned>(p.N));
+    if (grid.z > 65535u) {
+      // Split large batches into launches of at most 65535 images.
+      for (int n0 = 0; n0 < p.N; n0 += 65535) {
+        const int nb = p.N - n0 < 65535 ? p.N - n0 : 65535;
+        dim3 g2(grid.x, grid.y, static_cast<unsigned>(nb));
+        nchw_to_nhwc_kernel<XT><<<g2, 256, 0, st>>>(
+            reinterpret_cast<const XT*>(x) + size_t(n0) * p.C * HW,
+            x_nhwc + size_t(n0) * p.C * HW, p.C, HW);
+      }
+    } else {
+      nchw_to_nhwc_kernel<XT><<<grid, 256, 0, st>>>(reinterpret_cast<const XT*>(x), x_nhwc, p.C,
+                                                    HW);
+    }
+  }
+  // 2) weights -> swizzled B tiles (also clears the error word)
+  {
+    const size_t total = size_t(p.cchunks) * p.numKB * p.nrows * 8;
+    int64_t blocks = cdiv(static_cast<int64_t>(total), 256);
+    const int64_t cap = int64_t(di->sm_count) * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    pack_weights_kernel<PREC><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+        weight, wpack, err, p.O, p.C, p.T, p.Cg, p.CBg, p.numKB, p.nrows, p.cchunks);
+  }
+  // 3) the fused implicit GEMM
+  FusedArgs a;
+  a.x_nhwc = reinterpret_cast<const uint8_t*>(x_nhwc);
+  a.offset = offset; a.mask = mask; a.wpack = wpack; a.bias = bias; a.y = y; a.err = err;
+  a.N = p.N; a.C = p.C; a.H = p.H; a.W = p.W; a.O = p.O; a.Ho = p.Ho; a.Wo = p.Wo; a.P = p.P;
+  a.K = p.K; a.T = p.T; a.stride = p.stride; a.pad = p.pad; a.dil = p.dil; a.dg = p.dg;
+  a.Cg = p.Cg; a.CBg = p.CBg; a.numKB = p.numKB;
+  a.tiles_per_img = p.tiles_per_img; a.cchunks = p.cchunks; a.num_tiles = p.num_tiles;
+  a.n_mma = p.n_mma; a.nsub = p.nsub; a.nrows = p.nrows; a.acc_bufs = p.acc_bufs;
+  a.stages = p.stages; a.tmem_cols = p.tmem_cols;
+  a.a_stage_bytes = p.a_stage_bytes; a.b_stage_bytes = p.b_stage_bytes;
+  a.scale = scale; a.precise = p.precise ? 1 : 0; a.tf32_single = p.tf32_single ? 1 : 0;
+  a.timeout_ns = kDefaultTimeoutNs;
+  const int grid = p.num_tiles < di->sm_count ? p.num_tiles : di->sm_count;
+  dcnv2_fused_kernel<PREC><<<grid, kThreads, p.smem_bytes, st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
+}
+
+template <int PREC>
+dcnv2_status launch_simt(const Plan& p, DevInfo* di, const void* x, const void* offset,
+                         const void* mask, const void* weight, const void* bias, void* y,
+                         uint8_t* ws, float scale, cudaStream_t st) {
+  if (cudaMemsetAsync(ws, 0, sizeof(int), st) != cudaSuccess) return DCNV2_ERR_CUDA;
+  SimtArgs a;
+  a.x = x; a.offset = offset; a.mask = mask; a.w = weight; a.bias = bias; a.y = y;
+  a.N = p.N; a.C = p.C; a.H = p.H; a.W = p.W; a.O = p.O; a.Ho = p.Ho; a.Wo = p.Wo; a.P = p.P;
+  a.K = p.K; a.T = p.T; a.stride = p.stride; a.pad = p.pad; a.dil = p.dil; a.dg = p.dg;
+  a.Cg = p.Cg; a.scale = scale;
+  const size_t total = size_t(p.N) * p.O * p.P;
+  int64_t blocks = cdiv(static_cast<int64_t>(total), 256);
+  const int64_t cap = int64_t(di->sm_count) * 16;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  dcnv2_simt_kernel<PREC><<<static_cast<unsigned>(blocks), 256, 0, st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
+}
+
+bool aligned(const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; }
+
+// ---- failure-detection self test: a wait that nothing completes ----
+__global__ void selftest_timeout_kernel(int* err, unsigned long long timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(ptx::smem_addr(&bar), 1);
+    abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  FusedArgs a = {};
+  a.err = err;
+  a.timeout_ns = timeout_ns;
+  if (threadIdx.x == 0) {
+    // Parity 0 of a fresh barrier completes only after one arrival, which never comes.
+    if (!wait_bar(ptx::smem_addr(&bar), 0, a, &abort_flag, DCNV2_DEVERR_TIMEOUT_MMA)) {
+      // the error bit is already set by wait_bar
+    }
+    // Complete the phase so that the barrier is left in a clean state.
+    ptx::mbar_arrive(ptx::smem_addr(&bar));
+  }
+  __syncthreads();
+}
+
+}  // namespace
+}  // namespace dcnv2
+
+using namespace dcnv2;
+
+extern "C" {
+
+dcnv2_status dcnv2_output_shape(const dcnv2_desc* desc, int64_t out_dims[4]) {
+  if (!out_dims) return DCNV2_ERR_INVALID_ARG;
+  Plan p;
+  const dcnv2_status s = make_plan(desc, &p);
+  if (s != DCNV2_OK) return s;
+  out_dims[0] = p.N; out_dims[1] = p.O; out_dims[2] = p.Ho; out_dims[3] = p.Wo;
+  return DCNV2_OK;
+}
+
+size_t dcnv2_workspace_size(const dcnv2_desc* desc) {
+  Plan p;
+  if (make_plan(desc, &p) != DCNV2_OK) return 0;
+  return p.ws_bytes;
+}
+
+int32_t dcnv2_uses_tensor_cores(const dcnv2_desc* desc) {
+  Plan p;
+  if (make_plan(desc, &p) != DCNV2_OK) return 0;
+  return p.fused ? 1 : 0;
+}
+
+int32_t dcnv2_launch_count(const dcnv2_desc* desc) {
+  Plan p;
+  if (make_plan(desc, &p) != DCNV2_OK) return 0;
+  if (!p.fused) return 1;
+  const int64_t zsplits = (p.N + 65534) / 65535;
+  return static_cast<int32_t>(zsplits + 2);
+}
+
+dcnv2_status dcnv2_forward(const dcnv2_desc* desc, const void* x, const void* offset,
+                           const void* mask, const void* weight, const void* bias, void* y,
+                           void* workspace, size_t workspace_bytes, float x_scale, float w_scale,
+                           dcnv2_stream_t stream) {
+  Plan p;
+  dcnv2_status s = make_plan(desc, &p);
+  if (s != DCNV2_OK) return s;
+  if (!x || !offset || !mask || !weight || !y) return DCNV2_ERR_INVALID_ARG;
+  const size_t eb = static_cast<size_t>(p.elem_bytes);
+  const size_t gb = p.prec == PREC_F16 ? 2 : 4;  // offset / mask / bias / y elements
+  if (!aligned(x, eb) || !aligned(weight, eb) || !aligned(offset, gb) || !aligned(mask, gb) ||
+      !aligned(y, gb) || (bias && !aligned(bias, gb)))
+    return DCNV2_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < p.ws_bytes) return DCNV2_ERR_WORKSPACE;
+  float scale = 1.f;
+  if (p.prec == PREC_I8) {
+    if (!(x_scale > 0.f) || !(w_scale > 0.f) || !std::isfinite(x_scale) || !std::isfinite(w_scale))
+      return DCNV2_ERR_INVALID_ARG;
+    scale = x_scale * w_scale;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return DCNV2_ERR_NO_DEVICE; }
+  DevInfo* di = device_info(dev);
+  if (!di || !di->ok) return DCNV2_ERR_NO_DEVICE;
+  if (di->major != 10) return DCNV2_ERR_NO_DEVICE;  // built for sm_100a only
+  uint8_t* ws = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(workspace), 256));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (p.fused) {
+    switch (p.prec) {
+      case PREC_F16: return launch_fused<PREC_F16>(p, di, dev, x, offset, mask, weight, bias, y, ws, scale, st);
+      case PREC_I8: return launch_fused<PREC_I8>(p, di, dev, x, offset, mask, weight, bias, y, ws, scale, st);
+      default: return launch_fused<PREC_F32>(p, di, dev, x, offset, mask, weight, bias, y, ws, scale, st);
+    }
+  }
+  switch (p.prec) {
+    case PREC_F16: return launch_simt<PREC_F16>(p, di, x, offset, mask, weight, bias, y, ws, scale, st);
+    case PREC_I8: return launch_simt<PREC_I8>(p, di, x, offset, mask, weight, bias, y, ws, scale, st);
+    default: return launch_simt<PREC_F32>(p, di, x, offset, mask, weight, bias, y, ws, scale, st);
+  }
+}
+
+dcnv2_status dcnv2_read_device_error(const void* workspace, dcnv2_stream_t stream,
+                                     int32_t* code) {
+  if (!workspace || !code) return DCNV2_ERR_INVALID_ARG;
+  const uint8_t* ws =
+      reinterpret_cast<const uint8_t*>(align_up(reinterpret_cast<uintptr_t>(workspace), 256));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  if (cudaMemcpyAsync(&v, ws, sizeof(v), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess) {
+    cudaGetLastError();
+    return DCNV2_ERR_CUDA;
+  }
+  *code = v;
+  return v ? DCNV2_ERR_DEVICE_TIMEOUT : DCNV2_OK;
+}
+
+const char* dcnv2_status_string(dcnv2_status status) {
+  switch (status) {
+    case DCNV2_OK: return "ok";
+    case DCNV2_ERR_INVALID_ARG: return "invalid argument";
+    case DCNV2_ERR_UNSUPPORTED: return "unsupported dtype/format combination";
+    case DCNV2_ERR_WORKSPACE: return "workspace missing or too small";
+    case DCNV2_ERR_CUDA: return "CUDA runtime error";
+    case DCNV2_ERR_NO_DEVICE: return "no sm_100 device";
+    case DCNV2_ERR_DEVICE_TIMEOUT: return "kernel barrier wait timed out";
+  }
+  return "unknown status";
+}
+
+dcnv2_status dcnv2_diag_timeout_selftest(uint32_t timeout_us, int32_t* device_code) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return DCNV2_ERR_NO_DEVICE; }
+  DevInfo* di = device_info(dev);
+  if (!di || !di->ok || di->major != 10) return DCNV2_ERR_NO_DEVICE;
+  int* err = nullptr;
+  if (cudaMalloc(&err, sizeof(int)) != cudaSuccess) { cudaGetLastError(); return DCNV2_ERR_CUDA; }
+  dcnv2_status s = DCNV2_OK;
+  int v = 0;
+  if (cudaMemset(err, 0, sizeof(int)) != cudaSuccess) s = DCNV2_ERR_CUDA;
+  if (s == DCNV2_OK) {
+    selftest_timeout_kernel<<<1, 32>>>(err, 1000ull * timeout_us);
+    if (cudaGetLastError() != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+        cudaMemcpy(&v, err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+      s = DCNV2_ERR_CUDA;
+  }
+  cudaFree(err);
+  cudaGetLastError();
+  if (device_code) *device_code = v;
+  if (s != DCNV2_OK) return s;
+  return v ? DCNV2_ERR_DEVICE_TIMEOUT : DCNV2_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,754 @@
+// dcnv2_kernels.cuh — sm_100a DCNv2 forward kernels.
+//
+// The reference computes the forward in three launches per image (src/dcn_plugin.cpp:135-174):
+// a deformable im2col that writes the column matrix [C*K*K, Ho*Wo] to HBM
+// (src/dcn_kernel.cu:138-240), a cuBLAS GEMM, and a bias/scale pass (:168-178, :208-216,
+// :249-257). Here one persistent, warp-specialised implicit-GEMM kernel per precision does all
+// of it; the column matrix exists only as 128-byte-swizzled shared-memory tiles:
+//
+//   warp 0       producer: bulk-copies the pre-swizzled weight tile of each K-block into smem
+//   warp 1       MMA issuer: tcgen05.mma (kind::f16 / kind::i8 / kind::tf32) into TMEM,
+//                accumulator double-buffered so the epilogue overlaps the next tile
+//   warps 2-5    epilogue: tcgen05.ld from TMEM, + bias (x x_scale*w_scale for int8), store y
+//   warps 6-13   samplers: bilinear x mask samples of 128 output pixels x one K-block, written
+//                straight into the A-operand tile (one 16-byte chunk of channels per thread)
+//
+// GEMM view per tile: D[128 pixels, O] = A[128 pixels, C*K*K] * B[O, C*K*K]^T. K is ordered
+// (deformable group g, tap t, channel block) so that one K-block shares one sampling geometry;
+// the corner weights of a (pixel, tap, group) are computed once and reused for every channel
+// block of that group. x is read channels-last (a pre-pass transposes NCHW -> NHWC), so every
+// corner fetch is a 16-byte vector of 8 fp16 / 16 int8 / 4 fp32 channels.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/dcnv2.h"
+#include "ptx_sm100.cuh"
+
+namespace dcnv2 {
+
+enum Prec : int { PREC_F32 = 0, PREC_F16 = 1, PREC_I8 = 2 };
+
+constexpr int kTileM = 128;            // output pixels per tile (MMA M, TMEM lanes)
+constexpr int kRowBytes = 128;         // bytes of one operand row per K-block (128-byte swizzle)
+constexpr int kATileBytes = kTileM * kRowBytes;
+constexpr int kProducerWarp = 0;
+constexpr int kMmaWarp = 1;
+constexpr int kEpiWarp0 = 2;
+constexpr int kNumEpiWarps = 4;
+constexpr int kSampWarp0 = kEpiWarp0 + kNumEpiWarps;
+constexpr int kNumSampWarps = 8;
+constexpr int kThreads = (kSampWarp0 + kNumSampWarps) * 32;  // 448
+constexpr int kMaxStages = 8;
+constexpr int kRowsPerSampThread = kTileM * 8 / (kNumSampWarps * 32);  // 4
+
+template <int P> struct PrecTraits;
+template <> struct PrecTraits<PREC_F16> {
+  using X = __half;  // x, offset, mask, weight, bias, y
+  using G = __half;  // offset / mask element
+  using Y = __half;
+  static constexpr int kElemBytes = 2, kChunkElems = 8, kBlockElems = 64;
+  static constexpr int kNumATiles = 1, kNumBTiles = 1;
+};
+template <> struct PrecTraits<PREC_I8> {
+  using X = int8_t;
+  using G = float;
+  using Y = float;
+  static constexpr int kElemBytes = 1, kChunkElems = 16, kBlockElems = 128;
+  static constexpr int kNumATiles = 1, kNumBTiles = 1;
+};
+template <> struct PrecTraits<PREC_F32> {
+  using X = float;
+  using G = float;
+  using Y = float;
+  static constexpr int kElemBytes = 4, kChunkElems = 4, kBlockElems = 32;
+  static constexpr int kNumATiles = 2, kNumBTiles = 2;  // 3xTF32: hi and lo parts
+};
+
+struct FusedArgs {
+  const uint8_t* x_nhwc;   // [N][H][W][C] channels-last copy of x
+  const void* offset;      // [N][dg*2*T][Ho][Wo]
+  const void* mask;        // [N][dg*T][Ho][Wo]
+  const uint8_t* wpack;    // [cchunks][numKB][kNumBTiles][nrows][128 B], pre-swizzled
+  const void* bias;        // [O] or null
+  void* y;                 // [N][O][Ho][Wo]
+  int* err;                // device error word
+  int N, C, H, W, O, Ho, Wo, P;
+  int K, T, stride, pad, dil, dg, Cg, CBg, numKB;
+  int tiles_per_img, cchunks, num_tiles;
+  int n_mma, nsub, nrows, acc_bufs;
+  int stages;
+  uint32_t tmem_cols;
+  uint32_t a_stage_bytes, b_stage_bytes;
+  float scale;             // int8: x_scale * w_scale
+  int precise;             // fp16: fp32 sampler arithmetic
+  int tf32_single;         // fp32: hi*hi only (plain TF32)
+  unsigned long long timeout_ns;
+};
+
+// ------------------------------------------------------------------ bounded mbarrier wait
+// Spins on the barrier; gives up after timeout_ns (sets the CTA abort flag and the device
+// error word) or as soon as another role of this CTA has aborted.
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const FusedArgs& a,
+                                         volatile int* abort_flag, int code) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = ptx::global_timer_ns();
+  uint32_t n = 0;
+  while (true) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if ((++n & 31u) == 0) {
+      if (*abort_flag) return false;
+      if (ptx::global_timer_ns() - t0 > a.timeout_ns) {
+        *abort_flag = 1;
+        atomicOr(a.err, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void decode_tile(const FusedArgs& a, int tile, int& img, int& pt,
+                                            int& cc) {
+  cc = tile % a.cchunks;
+  const int r = tile / a.cchunks;
+  pt = r % a.tiles_per_img;
+  img = r / a.tiles_per_img;
+}
+
+// Geometry of one (pixel, tap, group): corner weights (mask folded in, zero when a corner is
+// outside the image or the sample centre is outside (-1, H) x (-1, W)) and the element offsets
+// of the four corner pixels inside the channels-last image (clamped, always readable).
+// Same rules as bilinear<T> in the reference (src/dcn_kernel.cu:19-30); the mask product is
+// applied to each corner weight instead of to the sum.
+struct Geom {
+  float a[4];
+  int off[4];
+};
+
+__device__ __forceinline__ Geom make_geom(const FusedArgs& a, bool valid, int base_h,
+                                          int base_w, float dh, float dw, float m) {
+  Geom g;
+  const float hf = __fadd_rn(static_cast<float>(base_h), dh);
+  const float wf = __fadd_rn(static_cast<float>(base_w), dw);
+  const bool inside = valid && !(hf <= -1.f || hf >= static_cast<float>(a.H) || wf <= -1.f ||
+                                 wf >= static_cast<float>(a.W));
+  const float h0f = floorf(hf), w0f = floorf(wf);
+  const int h0 = inside ? static_cast<int>(h0f) : 0;
+  const int w0 = inside ? static_cast<int>(w0f) : 0;
+  const float lh = __fsub_rn(hf, h0f), lw = __fsub_rn(wf, w0f);
+  const float hh = __fsub_rn(1.f, lh), hw = __fsub_rn(1.f, lw);
+  const bool hl_ok = h0 >= 0, wl_ok = w0 >= 0;
+  const bool hh_ok = h0 + 1 <= a.H - 1, wh_ok = w0 + 1 <= a.W - 1;
+  g.a[0] = (inside && hl_ok && wl_ok) ? __fmul_rn(m, __fmul_rn(hh, hw)) : 0.f;
+  g.a[1] = (inside && hl_ok && wh_ok) ? __fmul_rn(m, __fmul_rn(hh, lw)) : 0.f;
+  g.a[2] = (inside && hh_ok && wl_ok) ? __fmul_rn(m, __fmul_rn(lh, hw)) : 0.f;
+  g.a[3] = (inside && hh_ok && wh_ok) ? __fmul_rn(m, __fmul_rn(lh, lw)) : 0.f;
+  const int hc0 = min(max(h0, 0), a.H - 1), hc1 = min(max(h0 + 1, 0), a.H - 1);
+  const int wc0 = min(max(w0, 0), a.W - 1), wc1 = min(max(w0 + 1, 0), a.W - 1);
+  g.off[0] = (hc0 * a.W + wc0) * a.C;
+  g.off[1] = (hc0 * a.W + wc1) * a.C;
+  g.off[2] = (hc1 * a.W + wc0) * a.C;
+  g.off[3] = (hc1 * a.W + wc1) * a.C;
+  return g;
+}
+
+__device__ __forceinline__ float load_geom_value(const __half* p) { return __half2float(*p); }
+__device__ __forceinline__ float load_geom_value(const float* p) { return __ldg(p); }
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 v) {
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ __half2 bits_h2(uint32_t v) {
+  return *reinterpret_cast<__half2*>(&v);
+}
+
+// ---- per-precision chunk computation: 4 corner vectors -> one 16-byte operand chunk ----
+// fp16 fast path: packed half2 arithmetic, weights rounded to fp16.
+__device__ __forceinline__ uint32_t f16_mix_fast(uint32_t a0, uint32_t a1, uint32_t a2,
+                                                 uint32_t a3, uint32_t x0, uint32_t x1,
+                                                 uint32_t x2, uint32_t x3) {
+  __half2 v = __hmul2(bits_h2(a0), bits_h2(x0));
+  v = __hfma2(bits_h2(a1), bits_h2(x1), v);
+  v = __hfma2(bits_h2(a2), bits_h2(x2), v);
+  v = __hfma2(bits_h2(a3), bits_h2(x3), v);
+  return h2_bits(v);
+}
+// fp16 precise path: fp32 arithmetic, one rounding to fp16 per column value.
+__device__ __forceinline__ uint32_t f16_mix_precise(const float (&a)[4], uint32_t x0,
+                                                    uint32_t x1, uint32_t x2, uint32_t x3) {
+  const float2 f0 = __half22float2(bits_h2(x0)), f1 = __half22float2(bits_h2(x1));
+  const float2 f2 = __half22float2(bits_h2(x2)), f3 = __half22float2(bits_h2(x3));
+  float lo = __fmul_rn(a[0], f0.x), hi = __fmul_rn(a[0], f0.y);
+  lo = __fmaf_rn(a[1], f1.x, lo); hi = __fmaf_rn(a[1], f1.y, hi);
+  lo = __fmaf_rn(a[2], f2.x, lo); hi = __fmaf_rn(a[2], f2.y, hi);
+  lo = __fmaf_rn(a[3], f3.x, lo); hi = __fmaf_rn(a[3], f3.y, hi);
+  return h2_bits(__floats2half2_rn(lo, hi));
+}
+// int8: v = a0*x0 (+ a1*x1 + a2*x2 + a3*x3 by fma), c = clamp(rint(v), -127, 127).
+__device__ __forceinline__ uint32_t i8_mix_word(const float (&a)[4], uint32_t x0, uint32_t x1,
+                                                uint32_t x2, uint32_t x3) {
+  uint32_t out = 0;
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const int sh = 8 * b;
+    const float v0 = static_cast<float>(static_cast<int8_t>(x0 >> sh));
+    const float v1 = static_cast<float>(static_cast<int8_t>(x1 >> sh));
+    const float v2 = static_cast<float>(static_cast<int8_t>(x2 >> sh));
+    const float v3 = static_cast<float>(static_cast<int8_t>(x3 >> sh));
+    float v = __fmul_rn(a[0], v0);
+    v = __fmaf_rn(a[1], v1, v);
+    v = __fmaf_rn(a[2], v2, v);
+    v = __fmaf_rn(a[3], v3, v);
+    int q = __float2int_rn(v);
+    q = min(max(q, -127), 127);
+    out |= (static_cast<uint32_t>(q) & 0xFFu) << sh;
+  }
+  return out;
+}
+// fp32: same mixing order as int8, then the 3xTF32 split hi = tf32(v), lo = tf32(v - hi).
+__device__ __forceinline__ void f32_mix(const float (&a)[4], const uint4& x0, const uint4& x1,
+                                        const uint4& x2, const uint4& x3, uint4& hi, uint4& lo) {
+  const uint32_t* p0 = &x0.x; const uint32_t* p1 = &x1.x;
+  const uint32_t* p2 = &x2.x; const uint32_t* p3 = &x3.x;
+  uint32_t* ph = &hi.x; uint32_t* pl = &lo.x;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float v = __fmul_rn(a[0], __uint_as_float(p0[e]));
+    v = __fmaf_rn(a[1], __uint_as_float(p1[e]), v);
+    v = __fmaf_rn(a[2], __uint_as_float(p2[e]), v);
+    v = __fmaf_rn(a[3], __uint_as_float(p3[e]), v);
+    const uint32_t h = ptx::cvt_rna_tf32(v);
+    ph[e] = h;
+    pl[e] = ptx::cvt_rna_tf32(__fsub_rn(v, __uint_as_float(h)));
+  }
+}
+
+// ------------------------------------------------------------------ the fused kernel
+template <int PREC>
+__global__ void __launch_bounds__(kThreads, 1) dcnv2_fused_kernel(const FusedArgs args) {
+  using TR = PrecTraits<PREC>;
+  using GT = typename TR::G;
+  using YT = typename TR::Y;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = args.stages;
+  uint8_t* a_smem = smem;
+  uint8_t* b_smem = smem + S * args.a_stage_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(b_smem + S * args.b_stage_bytes);
+  const uint32_t full_a = ptx::smem_addr(bars);          // [S]
+  const uint32_t full_b = full_a + 8 * S;                // [S]
+  const uint32_t empty = full_b + 8 * S;                 // [S]
+  const uint32_t tfull = empty + 8 * S;                  // [2]
+  const uint32_t tempty = tfull + 16;                    // [2]
+  const uint32_t drain = tempty + 16;                    // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      ptx::mbar_init(full_a + 8 * s, kNumSampWarps);
+      ptx::mbar_init(full_b + 8 * s, 1);
+      ptx::mbar_init(empty + 8 * s, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(tfull + 8 * i, 1);
+      ptx::mbar_init(tempty + 8 * i, kNumEpiWarps);
+    }
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    ptx::tmem_alloc(ptx::smem_addr(tmem_slot), args.tmem_cols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------ producer (weights)
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      const uint32_t b_base = ptx::smem_addr(b_smem);
+      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
+        int img, pt, cc;
+        decode_tile(args, tile, img, pt, cc);
+        const uint8_t* src = args.wpack + static_cast<size_t>(cc) * args.numKB * args.b_stage_bytes;
+        for (int kb = 0; kb < args.numKB; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!wait_bar(empty + 8 * s, ph ^ 1, args, abort_flag, DCNV2_DEVERR_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(full_b + 8 * s, args.b_stage_bytes);
+          ptx::bulk_copy_g2s(b_base + s * args.b_stage_bytes,
+                             src + static_cast<size_t>(kb) * args.b_stage_bytes,
+                             args.b_stage_bytes, full_b + 8 * s);
+        }
+      }
+      // Wait for the copies still in flight (at most the last one per stage) before the CTA
+      // can exit and release its shared memory.
+      const int outstanding = it < S ? it : S;
+      for (int j = 0; j < outstanding; ++j) {
+        const int idx = it - 1 - j;
+        wait_bar(full_b + 8 * (idx % S), (idx / S) & 1, args, abort_flag, DCNV2_DEVERR_TIMEOUT_DRAIN);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t idesc;
+      if (PREC == PREC_F16) idesc = ptx::make_idesc(1, 0, args.n_mma);
+      else if (PREC == PREC_I8) idesc = ptx::make_idesc(2, 1, args.n_mma);
+      else idesc = ptx::make_idesc(1, 2, args.n_mma);
+      const uint32_t a_base = ptx::smem_addr(a_smem);
+      const uint32_t b_base = ptx::smem_addr(b_smem);
+      const uint32_t acc_cols = static_cast<uint32_t>(args.nrows);
+      int it = 0, tl = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x, ++tl) {
+        const int acc = tl % args.acc_bufs;
+        const uint32_t use = (tl / args.acc_bufs) & 1;
+        if (!wait_bar(tempty + 8 * acc, use ^ 1, args, abort_flag, DCNV2_DEVERR_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_base = tmem_base + acc * acc_cols;
+        for (int kb = 0; kb < args.numKB; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!wait_bar(full_a + 8 * s, ph, args, abort_flag, DCNV2_DEVERR_TIMEOUT_MMA) ||
+              !wait_bar(full_b + 8 * s, ph, args, abort_flag, DCNV2_DEVERR_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t a_s = a_base + s * args.a_stage_bytes;
+          const uint32_t b_s = b_base + s * args.b_stage_bytes;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = ptx::sw128_kmajor_desc(a_s + 32 * k);
+            for (int sub = 0; sub < args.nsub; ++sub) {
+              const uint32_t d = d_base + sub * args.n_mma;
+              const uint32_t b_off = b_s + sub * args.n_mma * kRowBytes + 32 * k;
+              const uint64_t bd = ptx::sw128_kmajor_desc(b_off);
+              const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+              if (PREC == PREC_F16) {
+                ptx::mma_f16(d, ad, bd, idesc, accum);
+              } else if (PREC == PREC_I8) {
+                ptx::mma_i8(d, ad, bd, idesc, accum);
+              } else {
+                ptx::mma_tf32(d, ad, bd, idesc, accum);
+                if (!args.tf32_single) {
+                  const uint64_t bd_lo =
+                      ptx::sw128_kmajor_desc(b_off + args.nrows * kRowBytes);
+                  const uint64_t ad_lo = ptx::sw128_kmajor_desc(a_s + kATileBytes + 32 * k);
+                  ptx::mma_tf32(d, ad, bd_lo, idesc, 1u);
+                  ptx::mma_tf32(d, ad_lo, bd, idesc, 1u);
+                }
+              }
+            }
+          }
+          ptx::tc_commit(empty + 8 * s);  // frees this stage once its MMAs have read it
+        }
+        if (!ok) break;
+        ptx::tc_commit(tfull + 8 * acc);  // accumulator ready for the epilogue
+      }
+      ptx::tc_commit(drain);
+      wait_bar(drain, 0, args, abort_flag, DCNV2_DEVERR_TIMEOUT_DRAIN);
+    }
+  } else if (warp < kSampWarp0) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const uint32_t acc_cols = static_cast<uint32_t>(args.nrows);
+    int tl = 0;
+    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++tl) {
+      const int acc = tl % args.acc_bufs;
+      const uint32_t ph = (tl / args.acc_bufs) & 1;
+      // Warp-uniform outcome: every lane must take part in the tcgen05.ld below or none.
+      const bool got = wait_bar(tfull + 8 * acc, ph, args, abort_flag, DCNV2_DEVERR_TIMEOUT_EPILOGUE);
+      if (!__all_sync(0xffffffffu, got)) break;
+      ptx::tc_fence_after();
+      int img, pt, cc;
+      decode_tile(args, tile, img, pt, cc);
+      const int p = pt * kTileM + q * 32 + lane;
+      const bool pvalid = p < args.P;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * acc_cols;
+      const int o_chunk = cc * args.nrows;
+      YT* yimg = reinterpret_cast<YT*>(args.y) + static_cast<size_t>(img) * args.O * args.P;
+      for (int col = 0; col < args.nrows; col += 16) {
+        const int o0 = o_chunk + col;
+        if (o0 >= args.O) break;  // warp-uniform
+        uint32_t r[16];
+        ptx::tmem_ld_32x32b_x16(taddr + col, r);
+        ptx::tmem_wait_ld();
+        if (pvalid) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int o = o0 + i;
+            if (o < args.O) {
+              YT* dst = yimg + static_cast<size_t>(o) * args.P + p;
+              if (PREC == PREC_F16) {
+                const float bo = args.bias
+                                     ? __half2float(reinterpret_cast<const __half*>(args.bias)[o])
+                                     : 0.f;
+                *reinterpret_cast<__half*>(dst) = __float2half_rn(__uint_as_float(r[i]) + bo);
+              } else if (PREC == PREC_I8) {
+                const float bo = args.bias ? __ldg(reinterpret_cast<const float*>(args.bias) + o)
+                                           : 0.f;
+                const float accf = __int2float_rn(static_cast<int>(r[i]));
+                *reinterpret_cast<float*>(dst) = __fmaf_rn(accf, args.scale, bo);
+              } else {
+                const float bo = args.bias ? __ldg(reinterpret_cast<const float*>(args.bias) + o)
+                                           : 0.f;
+                *reinterpret_cast<float*>(dst) = __uint_as_float(r[i]) + bo;
+              }
+            }
+          }
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(tempty + 8 * acc);
+    }
+  } else {
+    // ------------------------------------------------------------ samplers
+    constexpr int EPC = TR::kChunkElems, KC = TR::kBlockElems, EB = TR::kElemBytes;
+    const int st = threadIdx.x - kSampWarp0 * 32;
+    const int j = st & 7;       // 16-byte chunk of the 128-byte row
+    const int ps = st >> 3;     // pixel slot: rows ps + 32 r
+    const uint32_t a_base = ptx::smem_addr(a_smem);
+    const GT* offp = reinterpret_cast<const GT*>(args.offset);
+    const GT* maskp = reinterpret_cast<const GT*>(args.mask);
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
+      int img, pt, cc;
+      decode_tile(args, tile, img, pt, cc);
+      int pix[kRowsPerSampThread], oh[kRowsPerSampThread], ow[kRowsPerSampThread];
+      bool pval[kRowsPerSampThread];
+#pragma unroll
+      for (int r = 0; r < kRowsPerSampThread; ++r) {
+        pix[r] = pt * kTileM + ps + 32 * r;
+        pval[r] = pix[r] < args.P;
+        const int pc = pval[r] ? pix[r] : 0;
+        oh[r] = pc / args.Wo;
+        ow[r] = pc - oh[r] * args.Wo;
+      }
+      const uint8_t* ximg =
+          args.x_nhwc + static_cast<size_t>(img) * args.H * args.W * args.C * EB;
+      for (int g = 0; g < args.dg && ok; ++g) {
+        for (int t = 0; t < args.T && ok; ++t) {
+          const int ki = t / args.K, kj = t - ki * args.K;
+          const size_t goff =
+              (static_cast<size_t>(img) * args.dg + g) * 2 * args.T + 2 * t;
+          const size_t gmsk = (static_cast<size_t>(img) * args.dg + g) * args.T + t;
+          float wts[kRowsPerSampThread][4];
+          int cof[kRowsPerSampThread][4];
+#pragma unroll
+          for (int r = 0; r < kRowsPerSampThread; ++r) {
+            float dh = 0.f, dw = 0.f, m = 0.f;
+            if (pval[r]) {
+              dh = load_geom_value(offp + goff * args.P + pix[r]);
+              dw = load_geom_value(offp + (goff + 1) * args.P + pix[r]);
+              m = load_geom_value(maskp + gmsk * args.P + pix[r]);
+            }
+            const Geom gm = make_geom(args, pval[r], oh[r] * args.stride - args.pad + ki * args.dil,
+                                      ow[r] * args.stride - args.pad + kj * args.dil, dh, dw, m);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              wts[r][c] = gm.a[c];
+              cof[r][c] = gm.off[c];
+            }
+          }
+          uint32_t wh[kRowsPerSampThread][4];  // fp16 fast path: weights as duplicated half2
+          if (PREC == PREC_F16) {
+#pragma unroll
+            for (int r = 0; r < kRowsPerSampThread; ++r)
+#pragma unroll
+              for (int c = 0; c < 4; ++c) wh[r][c] = h2_bits(__float2half2_rn(wts[r][c]));
+          }
+          for (int cbg = 0; cbg < args.CBg; ++cbg, ++it) {
+            const int s = it % S;
+            const uint32_t ph = (it / S) & 1;
+            const bool got =
+                wait_bar(empty + 8 * s, ph ^ 1, args, abort_flag, DCNV2_DEVERR_TIMEOUT_SAMPLER);
+            if (!__all_sync(0xffffffffu, got)) {
+              ok = false;
+              break;
+            }
+            const int cig = cbg * KC + j * EPC;  // channel within the group
+            const bool cvalid = cig < args.Cg;
+            const int cbase = g * args.Cg + cig;
+            const uint32_t a_s = a_base + s * args.a_stage_bytes;
+#pragma unroll
+            for (int r = 0; r < kRowsPerSampThread; ++r) {
+              const int m_row = ps + 32 * r;
+              const uint32_t dst = a_s + m_row * kRowBytes + ((j ^ (m_row & 7)) << 4);
+              uint4 out = make_uint4(0, 0, 0, 0), out_lo = make_uint4(0, 0, 0, 0);
+              if (cvalid) {
+                const uint4 x0 = ptx::ld_nc_v4(ximg + static_cast<size_t>(cof[r][0] + cbase) * EB);
+                const uint4 x1 = ptx::ld_nc_v4(ximg + static_cast<size_t>(cof[r][1] + cbase) * EB);
+                const uint4 x2 = ptx::ld_nc_v4(ximg + static_cast<size_t>(cof[r][2] + cbase) * EB);
+                const uint4 x3 = ptx::ld_nc_v4(ximg + static_cast<size_t>(cof[r][3] + cbase) * EB);
+                if (PREC == PREC_F16) {
+                  if (args.precise) {
+                    out.x = f16_mix_precise(wts[r], x0.x, x1.x, x2.x, x3.x);
+                    out.y = f16_mix_precise(wts[r], x0.y, x1.y, x2.y, x3.y);
+                    out.z = f16_mix_precise(wts[r], x0.z, x1.z, x2.z, x3.z);
+                    out.w = f16_mix_precise(wts[r], x0.w, x1.w, x2.w, x3.w);
+                  } else {
+                    out.x = f16_mix_fast(wh[r][0], wh[r][1], wh[r][2], wh[r][3], x0.x, x1.x, x2.x, x3.x);
+                    out.y = f16_mix_fast(wh[r][0], wh[r][1], wh[r][2], wh[r][3], x0.y, x1.y, x2.y, x3.y);
+                    out.z = f16_mix_fast(wh[r][0], wh[r][1], wh[r][2], wh[r][3], x0.z, x1.z, x2.z, x3.z);
+                    out.w = f16_mix_fast(wh[r][0], wh[r][1], wh[r][2], wh[r][3], x0.w, x1.w, x2.w, x3.w);
+                  }
+                } else if (PREC == PREC_I8) {
+                  out.x = i8_mix_word(wts[r], x0.x, x1.x, x2.x, x3.x);
+                  out.y = i8_mix_word(wts[r], x0.y, x1.y, x2.y, x3.y);
+                  out.z = i8_mix_word(wts[r], x0.z, x1.z, x2.z, x3.z);
+                  out.w = i8_mix_word(wts[r], x0.w, x1.w, x2.w, x3.w);
+                } else {
+                  f32_mix(wts[r], x0, x1, x2, x3, out, out_lo);
+                }
+              }
+              ptx::st_shared_v4(dst, out);
+              if (PREC == PREC_F32) ptx::st_shared_v4(dst + kATileBytes, out_lo);
+            }
+            ptx::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(full_a + 8 * s);
+          }
+        }
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    __syncwarp();  // lane 0 ran the MMA loop alone; reconverge for the .sync.aligned dealloc
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, args.tmem_cols);
+  }
+}
+
+// ------------------------------------------------------------------ pre-pass: NCHW -> NHWC
+// One 32-bit word moves VEC = 4/sizeof(T) elements; tile = (32*VEC) channels x (32*VEC) pixels.
+template <typename T>
+__global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const T* __restrict__ x,
+                                                           T* __restrict__ xt, int C, int HW) {
+  constexpr int VEC = 4 / sizeof(T);
+  constexpr int TILE = 32 * VEC;
+  __shared__ T tile[TILE][TILE + VEC];
+  const int n = blockIdx.z;
+  const int c0 = blockIdx.y * TILE, p0 = blockIdx.x * TILE;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const T* xs = x + static_cast<size_t>(n) * C * HW;
+  T* xd = xt + static_cast<size_t>(n) * C * HW;
+  const bool vec_ok = (HW % VEC) == 0 && (p0 + TILE) <= HW &&
+                      (reinterpret_cast<uintptr_t>(x) & 3u) == 0;
+  for (int i = ty; i < TILE; i += 8) {
+    const int c = c0 + i;
+    if (c < C) {
+      const T* row = xs + static_cast<size_t>(c) * HW + p0;
+      if (vec_ok) {
+        const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(row) + tx);
+        const T* e = reinterpret_cast<const T*>(&w);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) tile[i][tx * VEC + k] = e[k];
+      } else {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) {
+          const int p = tx * VEC + k;
+          tile[i][p] = (p0 + p < HW) ? row[p] : T(0);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) tile[i][tx * VEC + k] = T(0);
+    }
+  }
+  __syncthreads();
+  const bool cvec_ok = (C % VEC) == 0 && (c0 + TILE) <= C &&
+                       (reinterpret_cast<uintptr_t>(xt) & 3u) == 0;
+  for (int i = ty; i < TILE; i += 8) {
+    const int p = p0 + i;
+    if (p >= HW) continue;
+    T* row = xd + static_cast<size_t>(p) * C + c0;
+    if (cvec_ok) {
+      uint32_t w;
+      T* e = reinterpret_cast<T*>(&w);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) e[k] = tile[tx * VEC + k][i];
+      reinterpret_cast<uint32_t*>(row)[tx] = w;
+    } else {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) {
+        const int c = tx * VEC + k;
+        if (c0 + c < C) row[c] = tile[c][i];
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ pre-pass: weight pack
+// Writes, for every (cout chunk, K-block), the B operand tile exactly as it must sit in shared
+// memory: row o (output channel), 16-byte chunk jc at chunk jc ^ (o % 8) of the 128-byte row.
+// K-block kb = (g*T + t)*CBg + cbg holds channels g*Cg + cbg*KC + [0, KC) of tap t.
+// Also clears the device error word for the fused kernel that follows.
+template <int PREC>
+__global__ void __launch_bounds__(256) pack_weights_kernel(const void* __restrict__ w,
+                                                           uint8_t* __restrict__ wpack,
+                                                           int* err, int O, int C, int T,
+                                                           int Cg, int CBg, int numKB,
+                                                           int nrows, int cchunks) {
+  using TR = PrecTraits<PREC>;
+  constexpr int EPC = TR::kChunkElems, KC = TR::kBlockElems;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *err = 0;
+  const size_t total = static_cast<size_t>(cchunks) * numKB * nrows * 8;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int jc = static_cast<int>(idx & 7);
+    const int row = static_cast<int>((idx >> 3) % nrows);
+    const size_t blk = (idx >> 3) / nrows;  // cc * numKB + kb
+    const int kb = static_cast<int>(blk % numKB);
+    const int cc = static_cast<int>(blk / numKB);
+    const int cbg = kb % CBg;
+    const int t = (kb / CBg) % T;
+    const int g = kb / (CBg * T);
+    const int o = cc * nrows + row;
+    const size_t tile_base = blk * TR::kNumBTiles * nrows * kRowBytes;
+    const size_t dst = tile_base + static_cast<size_t>(row) * kRowBytes + ((jc ^ (row & 7)) << 4);
+    uint4 hi = make_uint4(0, 0, 0, 0), lo = make_uint4(0, 0, 0, 0);
+    uint8_t* hb = reinterpret_cast<uint8_t*>(&hi);
+    uint8_t* lb = reinterpret_cast<uint8_t*>(&lo);
+#pragma unroll
+    for (int e = 0; e < EPC; ++e) {
+      const int cig = cbg * KC + jc * EPC + e;
+      if (o < O && cig < Cg) {
+        const size_t src = (static_cast<size_t>(o) * C + g * Cg + cig) * T + t;
+        if (PREC == PREC_F16) {
+          reinterpret_cast<__half*>(hb)[e] = reinterpret_cast<const __half*>(w)[src];
+        } else if (PREC == PREC_I8) {
+          reinterpret_cast<int8_t*>(hb)[e] = reinterpret_cast<const int8_t*>(w)[src];
+        } else {
+          const float v = reinterpret_cast<const float*>(w)[src];
+          const uint32_t h = ptx::cvt_rna_tf32(v);
+          reinterpret_cast<uint32_t*>(hb)[e] = h;
+          reinterpret_cast<uint32_t*>(lb)[e] = ptx::cvt_rna_tf32(v - __uint_as_float(h));
+        }
+      }
+    }
+    *reinterpret_cast<uint4*>(wpack + dst) = hi;
+    if (TR::kNumBTiles == 2)
+      *reinterpret_cast<uint4*>(wpack + dst + static_cast<size_t>(nrows) * kRowBytes) = lo;
+  }
+}
+
+// ------------------------------------------------------------------ CUDA-core fallback
+// One thread per output element, any shape (the reference's naive kernel structure,
+// src/dcn_kernel.cu:33-65, extended to N, groups and the int8 requantisation). Column values use
+// the same geometry and mixing order as the fused kernels; fp16 columns are rounded to fp16.
+struct SimtArgs {
+  const void* x; const void* offset; const void* mask; const void* w; const void* bias; void* y;
+  int N, C, H, W, O, Ho, Wo, P, K, T, stride, pad, dil, dg, Cg;
+  float scale;
+};
+
+template <int PREC>
+__global__ void __launch_bounds__(256) dcnv2_simt_kernel(const SimtArgs a) {
+  using TR = PrecTraits<PREC>;
+  using XT = typename TR::X;
+  using GT = typename TR::G;
+  const size_t total = static_cast<size_t>(a.N) * a.O * a.P;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int p = static_cast<int>(idx % a.P);
+    const int o = static_cast<int>((idx / a.P) % a.O);
+    const int n = static_cast<int>(idx / (static_cast<size_t>(a.P) * a.O));
+    const int oh = p / a.Wo, ow = p - (p / a.Wo) * a.Wo;
+    const XT* xn = reinterpret_cast<const XT*>(a.x) + static_cast<size_t>(n) * a.C * a.H * a.W;
+    const GT* offp = reinterpret_cast<const GT*>(a.offset);
+    const GT* maskp = reinterpret_cast<const GT*>(a.mask);
+    float facc = 0.f;
+    long long iacc = 0;
+    for (int g = 0; g < a.dg; ++g) {
+      for (int t = 0; t < a.T; ++t) {
+        const int ki = t / a.K, kj = t - ki * a.K;
+        const size_t goff = (static_cast<size_t>(n) * a.dg + g) * 2 * a.T + 2 * t;
+        const size_t gmsk = (static_cast<size_t>(n) * a.dg + g) * a.T + t;
+        const float dh = load_geom_value(offp + goff * a.P + p);
+        const float dw = load_geom_value(offp + (goff + 1) * a.P + p);
+        const float m = load_geom_value(maskp + gmsk * a.P + p);
+        const float hf = __fadd_rn(static_cast<float>(oh * a.stride - a.pad + ki * a.dil), dh);
+        const float wf = __fadd_rn(static_cast<float>(ow * a.stride - a.pad + kj * a.dil), dw);
+        const bool inside = !(hf <= -1.f || hf >= static_cast<float>(a.H) || wf <= -1.f ||
+                              wf >= static_cast<float>(a.W));
+        float wt[4] = {0.f, 0.f, 0.f, 0.f};
+        int idx4[4] = {-1, -1, -1, -1};
+        if (inside) {
+          const float h0f = floorf(hf), w0f = floorf(wf);
+          const int h0 = static_cast<int>(h0f), w0 = static_cast<int>(w0f);
+          const float lh = __fsub_rn(hf, h0f), lw = __fsub_rn(wf, w0f);
+          const float hh = __fsub_rn(1.f, lh), hw = __fsub_rn(1.f, lw);
+          if (h0 >= 0 && w0 >= 0) { wt[0] = __fmul_rn(m, __fmul_rn(hh, hw)); idx4[0] = h0 * a.W + w0; }
+          if (h0 >= 0 && w0 + 1 <= a.W - 1) { wt[1] = __fmul_rn(m, __fmul_rn(hh, lw)); idx4[1] = h0 * a.W + w0 + 1; }
+          if (h0 + 1 <= a.H - 1 && w0 >= 0) { wt[2] = __fmul_rn(m, __fmul_rn(lh, hw)); idx4[2] = (h0 + 1) * a.W + w0; }
+          if (h0 + 1 <= a.H - 1 && w0 + 1 <= a.W - 1) { wt[3] = __fmul_rn(m, __fmul_rn(lh, lw)); idx4[3] = (h0 + 1) * a.W + w0 + 1; }
+        }
+        for (int ci = 0; ci < a.Cg; ++ci) {
+          const int c = g * a.Cg + ci;
+          const XT* plane = xn + static_cast<size_t>(c) * a.H * a.W;
+          float xv[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (idx4[k] >= 0) {
+              if (PREC == PREC_F16) xv[k] = __half2float(reinterpret_cast<const __half*>(plane)[idx4[k]]);
+              else if (PREC == PREC_I8) xv[k] = static_cast<float>(reinterpret_cast<const int8_t*>(plane)[idx4[k]]);
+              else xv[k] = reinterpret_cast<const float*>(plane)[idx4[k]];
+            } else {
+              xv[k] = 0.f;
+            }
+          }
+          float v = __fmul_rn(wt[0], xv[0]);
+          v = __fmaf_rn(wt[1], xv[1], v);
+          v = __fmaf_rn(wt[2], xv[2], v);
+          v = __fmaf_rn(wt[3], xv[3], v);
+          const size_t widx = (static_cast<size_t>(o) * a.C + c) * a.T + t;
+          if (PREC == PREC_I8) {
+            int q = __float2int_rn(v);
+            q = min(max(q, -127), 127);
+            iacc += static_cast<long long>(q) * reinterpret_cast<const int8_t*>(a.w)[widx];
+          } else if (PREC == PREC_F16) {
+            const float cv = __half2float(__float2half_rn(v));
+            facc = __fmaf_rn(__half2float(reinterpret_cast<const __half*>(a.w)[widx]), cv, facc);
+          } else {
+            facc = __fmaf_rn(reinterpret_cast<const float*>(a.w)[widx], v, facc);
+          }
+        }
+      }
+    }
+    if (PREC == PREC_F16) {
+      const float bo = a.bias ? __half2float(reinterpret_cast<const __half*>(a.bias)[o]) : 0.f;
+      reinterpret_cast<__half*>(a.y)[idx] = __float2half_rn(facc + bo);
+    } else if (PREC == PREC_I8) {
+      const float bo = a.bias ? reinterpret_cast<const float*>(a.bias)[o] : 0.f;
+      reinterpret_cast<float*>(a.y)[idx] =
+          __fmaf_rn(static_cast<float>(iacc), a.scale, bo);
+    } else {
+      const float bo = a.bias ? reinterpret_cast<const float*>(a.bias)[o] : 0.f;
+      reinterpret_cast<float*>(a.y)[idx] = facc + bo;
+    }
+  }
+}
+
+}  // namespace dcnv2

@@ -1,0 +1,171 @@
+"""ctypes binding of libdcnv2.so (include/dcnv2.h).
+
+This is the Python-side FFI a caller of the reference would write around libdcnv2.so
+(python/02_build_and_validate.py:29 loads it with ctypes.CDLL). It adds nothing to the compute
+path: every forward goes through the C ABI into the sm_100a kernels. If the library is missing the
+import of this module fails loudly; there is no fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import enum
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.normpath(os.path.join(_HERE, "..", "lib", "libdcnv2.so"))
+
+
+class Status(enum.IntEnum):
+    OK = 0
+    ERR_INVALID_ARG = 1
+    ERR_UNSUPPORTED = 2
+    ERR_WORKSPACE = 3
+    ERR_CUDA = 4
+    ERR_NO_DEVICE = 5
+    ERR_DEVICE_TIMEOUT = 6
+
+
+class DType(enum.IntEnum):
+    """Values of nvinfer1::DataType used by the plugin."""
+    FLOAT = 0
+    HALF = 1
+    INT8 = 2
+
+
+class Math(enum.IntEnum):
+    DEFAULT = 0
+    PRECISE = 1
+    TF32 = 2
+    SIMT = 3
+
+
+FORMAT_LINEAR = 0
+
+
+class Desc(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "n", "c", "h", "w", "out_c", "kernel", "stride", "padding", "dilation",
+        "deformable_groups", "dtype", "math")]
+
+
+class TensorDesc(ctypes.Structure):
+    _fields_ = [("nb_dims", ctypes.c_int32), ("d", ctypes.c_int64 * 8), ("type", ctypes.c_int32),
+                ("format", ctypes.c_int32), ("scale", ctypes.c_float)]
+
+
+class DCNv2Error(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        self.status = Status(status) if status in Status._value2member_map_ else status
+        super().__init__(f"{what}: {self.status!r}" if what else repr(self.status))
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"libdcnv2.so not built at {LIB_PATH}; run __graft_entry__.build()")
+    lib = ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_GLOBAL)
+    P = ctypes.c_void_p
+    Dp = ctypes.POINTER(Desc)
+    TDp = ctypes.POINTER(TensorDesc)
+    sig = {
+        "dcnv2_output_shape": (ctypes.c_int, [Dp, ctypes.POINTER(ctypes.c_int64)]),
+        "dcnv2_workspace_size": (ctypes.c_size_t, [Dp]),
+        "dcnv2_forward": (ctypes.c_int, [Dp, P, P, P, P, P, P, P, ctypes.c_size_t, ctypes.c_float,
+                                         ctypes.c_float, P]),
+        "dcnv2_read_device_error": (ctypes.c_int, [P, P, ctypes.POINTER(ctypes.c_int32)]),
+        "dcnv2_uses_tensor_cores": (ctypes.c_int32, [Dp]),
+        "dcnv2_launch_count": (ctypes.c_int32, [Dp]),
+        "dcnv2_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+        "dcnv2_plugin_name": (ctypes.c_char_p, []),
+        "dcnv2_plugin_version": (ctypes.c_char_p, []),
+        "dcnv2_plugin_namespace": (ctypes.c_char_p, []),
+        "dcnv2_plugin_field_names": (ctypes.c_int32, [ctypes.POINTER(ctypes.POINTER(ctypes.c_char_p))]),
+        "dcnv2_plugin_create": (P, [ctypes.POINTER(ctypes.c_char_p),
+                                    ctypes.POINTER(ctypes.POINTER(ctypes.c_int32)), ctypes.c_int32]),
+        "dcnv2_plugin_clone": (P, [P]),
+        "dcnv2_plugin_destroy": (None, [P]),
+        "dcnv2_plugin_serialize": (ctypes.c_int32, [P, ctypes.POINTER(ctypes.c_char_p),
+                                                    ctypes.POINTER(ctypes.c_int32)]),
+        "dcnv2_plugin_nb_outputs": (ctypes.c_int32, [P]),
+        "dcnv2_plugin_output_dtype": (ctypes.c_int32, [P, ctypes.c_int32]),
+        "dcnv2_plugin_output_shape": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_int64),
+                                                     ctypes.POINTER(ctypes.c_int64),
+                                                     ctypes.POINTER(ctypes.c_int64)]),
+        "dcnv2_plugin_supports_format": (ctypes.c_int32, [P, ctypes.c_int32, TDp, ctypes.c_int32,
+                                                          ctypes.c_int32]),
+        "dcnv2_plugin_workspace_size": (ctypes.c_size_t, [P, TDp, ctypes.c_int32, TDp,
+                                                          ctypes.c_int32]),
+        "dcnv2_plugin_enqueue": (ctypes.c_int32, [P, TDp, TDp, ctypes.POINTER(P),
+                                                  ctypes.POINTER(P), P, ctypes.c_size_t, P]),
+        "dcnv2_diag_timeout_selftest": (ctypes.c_int, [ctypes.c_uint32,
+                                                       ctypes.POINTER(ctypes.c_int32)]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+#: Every entry point include/dcnv2.h and include/dcnv2_diag.h declare.
+EXPORTED = (
+    "dcnv2_output_shape", "dcnv2_workspace_size", "dcnv2_forward", "dcnv2_read_device_error",
+    "dcnv2_uses_tensor_cores", "dcnv2_launch_count", "dcnv2_status_string", "dcnv2_plugin_name",
+    "dcnv2_plugin_version", "dcnv2_plugin_namespace", "dcnv2_plugin_field_names",
+    "dcnv2_plugin_create", "dcnv2_plugin_clone", "dcnv2_plugin_destroy",
+    "dcnv2_plugin_serialize", "dcnv2_plugin_nb_outputs", "dcnv2_plugin_output_dtype",
+    "dcnv2_plugin_output_shape", "dcnv2_plugin_supports_format", "dcnv2_plugin_workspace_size",
+    "dcnv2_plugin_enqueue", "dcnv2_diag_timeout_selftest",
+)
+
+
+def make_desc(n, c, h, w, out_c, kernel=3, stride=1, padding=1, dilation=1,
+              deformable_groups=1, dtype=DType.HALF, math=Math.DEFAULT) -> Desc:
+    return Desc(int(n), int(c), int(h), int(w), int(out_c), int(kernel), int(stride),
+                int(padding), int(dilation), int(deformable_groups), int(dtype), int(math))
+
+
+def output_shape(desc: Desc):
+    out = (ctypes.c_int64 * 4)()
+    st = lib.dcnv2_output_shape(ctypes.byref(desc), out)
+    if st != Status.OK:
+        raise DCNv2Error(st, "dcnv2_output_shape")
+    return tuple(out)
+
+
+def workspace_size(desc: Desc) -> int:
+    return int(lib.dcnv2_workspace_size(ctypes.byref(desc)))
+
+
+def uses_tensor_cores(desc: Desc) -> bool:
+    return bool(lib.dcnv2_uses_tensor_cores(ctypes.byref(desc)))
+
+
+def launch_count(desc: Desc) -> int:
+    return int(lib.dcnv2_launch_count(ctypes.byref(desc)))
+
+
+def forward_raw(desc: Desc, x, offset, mask, weight, bias, y, workspace, workspace_bytes,
+                x_scale=1.0, w_scale=1.0, stream=0) -> int:
+    """Raw C call with integer device addresses; returns the dcnv2_status value."""
+    return int(lib.dcnv2_forward(ctypes.byref(desc), x, offset, mask, weight, bias, y, workspace,
+                                 workspace_bytes, float(x_scale), float(w_scale), stream))
+
+
+def read_device_error(workspace, stream=0) -> int:
+    code = ctypes.c_int32(0)
+    st = lib.dcnv2_read_device_error(workspace, stream, ctypes.byref(code))
+    if st not in (Status.OK, Status.ERR_DEVICE_TIMEOUT):
+        raise DCNv2Error(st, "dcnv2_read_device_error")
+    return int(code.value)
+
+
+def status_string(st: int) -> str:
+    return lib.dcnv2_status_string(int(st)).decode()
+
+
+def timeout_selftest(timeout_us: int):
+    code = ctypes.c_int32(0)
+    st = lib.dcnv2_diag_timeout_selftest(int(timeout_us), ctypes.byref(code))
+    return int(st), int(code.value)

@@ -1,0 +1,178 @@
+"""Host-side checks of libdcnv2.so that need no GPU: the library loads, exports every symbol the
+headers declare, and its plugin logic (identity, attributes, serialisation, shape inference,
+precision negotiation, workspace rule, argument validation) behaves like the reference plugin
+(src/dcn_plugin.cpp). No kernel is launched here."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from dcnv2_b200 import DCNv2Creator, tensor_desc
+from dcnv2_b200 import capi
+from dcnv2_b200.capi import DType, Math, Status
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for h in ("dcnv2.h", "dcnv2_diag.h"):
+        src = open(os.path.join(ROOT, "include", h)).read()
+        names |= set(re.findall(r"DCNV2_API\s+[\w\s\*]+?\b(dcnv2_\w+)\s*\(", src))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    names = declared_symbols()
+    assert len(names) >= 20
+    lib = ctypes.CDLL(capi.LIB_PATH)
+    for n in sorted(names):
+        assert hasattr(lib, n), n
+    assert names == set(capi.EXPORTED)
+
+
+def test_library_is_sm100a_only():
+    data = open(capi.LIB_PATH, "rb").read()
+    assert b"sm_100a" in data
+
+
+def test_plugin_identity_and_fields():
+    cr = DCNv2Creator()
+    assert (cr.get_plugin_name(), cr.get_plugin_version(), cr.get_plugin_namespace()) == \
+        ("DCNv2", "1", "")
+    assert cr.get_field_names() == ["stride", "padding", "dilation", "kernel",
+                                    "deformable_groups"]
+    p = cr.create_plugin("DCNv2", {})
+    assert p.get_fields_to_serialize() == {"stride": 1, "padding": 1, "dilation": 1,
+                                           "kernel": 3, "deformable_groups": 1}
+    p2 = cr.create_plugin("DCNv2", {"stride": 2, "padding": 2, "dilation": 2, "kernel": 5,
+                                    "deformable_groups": 8, "unknown": 7})
+    f = p2.get_fields_to_serialize()
+    assert f == {"stride": 2, "padding": 2, "dilation": 2, "kernel": 5, "deformable_groups": 8}
+    # a field without data reads as 0 (src/dcn_plugin.cpp:227)
+    assert cr.create_plugin("DCNv2", {"padding": None}).get_fields_to_serialize()["padding"] == 0
+    # serialize -> create round trip
+    assert cr.create_plugin("DCNv2", f).get_fields_to_serialize() == f
+    assert p2.clone().get_fields_to_serialize() == f
+    assert p2.attach_to_context().get_fields_to_serialize() == f
+    assert p.get_nb_outputs() == 1
+
+
+@pytest.mark.parametrize("attrs,x,w,expect", [
+    (dict(), (1, 256, 64, 64), (256, 256, 3, 3), (1, 256, 64, 64)),
+    (dict(stride=2), (2, 16, 11, 13), (24, 16, 3, 3), (2, 24, 6, 7)),
+    (dict(padding=2, dilation=2), (1, 512, 128, 128), (512, 512, 3, 3), (1, 512, 128, 128)),
+    (dict(kernel=1, padding=0), (3, 8, 7, 9), (4, 8, 1, 1), (3, 4, 7, 9)),
+    (dict(kernel=5, padding=2, stride=3), (1, 8, 10, 17), (8, 8, 5, 5), (1, 8, 4, 6)),
+])
+def test_output_shapes(attrs, x, w, expect):
+    p = DCNv2Creator().create_plugin("DCNv2", attrs)
+    assert p.get_output_shapes(x, w) == [expect]
+    d = capi.make_desc(*x, w[0], kernel=attrs.get("kernel", 3), stride=attrs.get("stride", 1),
+                       padding=attrs.get("padding", 1), dilation=attrs.get("dilation", 1))
+    assert capi.output_shape(d) == expect
+
+
+def test_supports_format_combination():
+    p = DCNv2Creator().create_plugin("DCNv2", {})
+    F, H, I = DType.FLOAT, DType.HALF, DType.INT8
+
+    def combo(types, fmt=0):
+        return [tensor_desc((1, 1, 1, 1), t, fmt) for t in types]
+
+    for t in (F, H, I):
+        assert p.supports_format_combination(0, combo([t] * 6))
+    assert not p.supports_format_combination(0, combo([F] * 6, fmt=1))  # non-linear format
+    assert all(p.supports_format_combination(i, combo([H] * 6)) for i in range(6))
+    assert not p.supports_format_combination(3, combo([H, H, H, F, H, H]))
+    int8 = combo([I, F, F, I, F, F])
+    assert all(p.supports_format_combination(i, int8) for i in range(6))
+    assert not p.supports_format_combination(5, combo([I, F, F, I, F, I]))
+    assert not p.supports_format_combination(1, combo([I, I, F, I, F, F]))
+    # output dtype follows x, except INT8 -> FLOAT (agrees with the combination above)
+    assert p.get_output_data_types([F]) == [F]
+    assert p.get_output_data_types([H]) == [H]
+    assert p.get_output_data_types([I]) == [F]
+
+
+def test_workspace_rule():
+    d = capi.make_desc(64, 256, 64, 64, 256, dtype=DType.HALF)
+    ws = capi.workspace_size(d)
+    x_bytes = 64 * 256 * 64 * 64 * 2
+    w_bytes = 9 * 4 * 256 * 128  # 36 K-blocks x 256 rows x 128 B
+    assert x_bytes + w_bytes <= ws <= x_bytes + w_bytes + 4096
+    assert capi.uses_tensor_cores(d)
+    assert capi.launch_count(d) == 3
+    # scales with N (the reference's rule ignored N)
+    d1 = capi.make_desc(1, 256, 64, 64, 256, dtype=DType.HALF)
+    assert capi.workspace_size(d1) < ws
+    # plugin path agrees with the desc path
+    p = DCNv2Creator().create_plugin("DCNv2", {})
+    ins = [tensor_desc((64, 256, 64, 64), DType.HALF), tensor_desc((64, 18, 64, 64), DType.HALF),
+           tensor_desc((64, 9, 64, 64), DType.HALF), tensor_desc((256, 256, 3, 3), DType.HALF),
+           tensor_desc((256,), DType.HALF)]
+    outs = [tensor_desc((64, 256, 64, 64), DType.HALF)]
+    assert p.get_workspace_size(ins, outs) == ws
+    # SIMT-only shapes need just the error word
+    odd = capi.make_desc(1, 6, 9, 9, 4, dtype=DType.HALF)
+    assert not capi.uses_tensor_cores(odd) and capi.workspace_size(odd) <= 1024
+    assert capi.launch_count(odd) == 1
+
+
+@pytest.mark.parametrize("kw", [
+    dict(n=0), dict(c=0), dict(h=0), dict(out_c=0), dict(kernel=0), dict(stride=0),
+    dict(padding=-1), dict(dilation=0), dict(deformable_groups=0), dict(deformable_groups=3),
+    dict(h=1, w=1, padding=0), dict(math=9),
+])
+def test_invalid_descs(kw):
+    base = dict(n=1, c=16, h=8, w=8, out_c=8)
+    base.update(kw)
+    n, c, h, w, o = (base.pop(k) for k in ("n", "c", "h", "w", "out_c"))
+    d = capi.make_desc(n, c, h, w, o, **base)
+    assert capi.workspace_size(d) == 0
+    st = capi.forward_raw(d, 16, 16, 16, 16, 16, 16, 256, 1 << 20)
+    assert st == Status.ERR_INVALID_ARG
+
+
+def test_forward_argument_errors_before_any_launch():
+    d = capi.make_desc(1, 16, 8, 8, 8, dtype=DType.FLOAT)
+    wsz = capi.workspace_size(d)
+    assert capi.forward_raw(d, None, 256, 256, 256, 256, 256, 256, wsz) == Status.ERR_INVALID_ARG
+    assert capi.forward_raw(d, 258, 256, 256, 256, 256, 256, 256, wsz) == Status.ERR_INVALID_ARG
+    assert capi.forward_raw(d, 256, 256, 256, 256, 256, 256, None, wsz) == Status.ERR_WORKSPACE
+    assert capi.forward_raw(d, 256, 256, 256, 256, 256, 256, 256, wsz - 1) == Status.ERR_WORKSPACE
+    d8 = capi.make_desc(1, 16, 8, 8, 8, dtype=DType.INT8)
+    for xs, ws in ((0.0, 1.0), (1.0, -1.0), (float("nan"), 1.0), (float("inf"), 1.0)):
+        assert capi.forward_raw(d8, 256, 256, 256, 256, 256, 256, 256,
+                                capi.workspace_size(d8), xs, ws) == Status.ERR_INVALID_ARG
+    bad = capi.make_desc(1, 16, 8, 8, 8, dtype=7)
+    assert capi.forward_raw(bad, 256, 256, 256, 256, 256, 256, 256, 1 << 20) == \
+        Status.ERR_UNSUPPORTED
+    assert capi.status_string(Status.ERR_WORKSPACE).startswith("workspace")
+
+
+def test_math_modes_select_kernels():
+    f32 = capi.make_desc(1, 256, 64, 64, 256, dtype=DType.FLOAT)
+    assert capi.uses_tensor_cores(f32)
+    simt = capi.make_desc(1, 256, 64, 64, 256, dtype=DType.FLOAT, math=Math.SIMT)
+    assert not capi.uses_tensor_cores(simt)
+    tf32_on_half = capi.make_desc(1, 256, 64, 64, 256, dtype=DType.HALF, math=Math.TF32)
+    assert capi.workspace_size(tf32_on_half) == 0
+    # int8 needs 16-channel groups for the tensor-core path
+    assert capi.uses_tensor_cores(capi.make_desc(1, 32, 8, 8, 8, dtype=DType.INT8))
+    assert not capi.uses_tensor_cores(capi.make_desc(1, 24, 8, 8, 8, dtype=DType.INT8))
+    assert capi.uses_tensor_cores(capi.make_desc(1, 24, 8, 8, 8, dtype=DType.HALF))
+
+
+def test_enqueue_rejects_mismatched_output_and_combination():
+    p = DCNv2Creator().create_plugin("DCNv2", {})
+    H = DType.HALF
+    ins = [tensor_desc((1, 16, 8, 8), H), tensor_desc((1, 18, 8, 8), H),
+           tensor_desc((1, 9, 8, 8), H), tensor_desc((8, 16, 3, 3), H), tensor_desc((8,), H)]
+    bad_out = [tensor_desc((1, 8, 7, 8), H)]
+    assert p.enqueue(ins, bad_out, [256] * 5, [256], 256, 1 << 20) == Status.ERR_INVALID_ARG
+    mixed = list(ins)
+    mixed[1] = tensor_desc((1, 18, 8, 8), DType.FLOAT)
+    assert p.enqueue(mixed, [tensor_desc((1, 8, 8, 8), H)], [256] * 5, [256], 256, 1 << 20) == \
+        Status.ERR_UNSUPPORTED
