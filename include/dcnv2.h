@@ -61,10 +61,12 @@ typedef enum {
 
 /* Math modes (dcnv2_desc.math). */
 enum {
-  DCNV2_MATH_DEFAULT = 0,    /* fp16: packed-f16 sampler; fp32: 3xTF32 split (fp32-exact); int8: exact */
-  DCNV2_MATH_PRECISE = 1,    /* fp16: fp32 sampler arithmetic (one rounding of each column value) */
-  DCNV2_MATH_TF32 = 2,       /* fp32 only: single-pass TF32 tensor cores (reported separately) */
-  DCNV2_MATH_SIMT = 3        /* force the CUDA-core kernel (any shape; used as a cross-check) */
+  DCNV2_MATH_DEFAULT = 0,    /* fp16: tensor cores, packed-f16 sampler; int8: tensor cores, exact
+                                int32 accumulation; fp32: fused CUDA-core kernel, fp32-exact */
+  DCNV2_MATH_PRECISE = 1,    /* fp16: fp32 sampler arithmetic (one rounding per column value) */
+  DCNV2_MATH_TF32 = 2,       /* fp32 only: single-pass TF32 tensor cores (own, looser bound) */
+  DCNV2_MATH_SIMT = 3,       /* one thread per output on CUDA cores (any shape; cross-check) */
+  DCNV2_MATH_TF32X3 = 4      /* fp32 only: 3xTF32 split on tensor cores (own bound, ~5e-5 rel.) */
 };
 
 /* Layer description: shapes of x and weight plus the five plugin attributes. */
@@ -112,7 +114,8 @@ enum {
   DCNV2_DEVERR_TIMEOUT_DRAIN = 16
 };
 
-/* Which kernel family dcnv2_forward would launch: 1 = fused tcgen05, 0 = CUDA-core fallback. */
+/* Which kernel family dcnv2_forward would launch: 1 = fused tcgen05 (tensor cores),
+ * 2 = fused fp32-exact CUDA-core kernel, 0 = one-thread-per-output CUDA-core kernel. */
 DCNV2_API int32_t dcnv2_uses_tensor_cores(const dcnv2_desc* desc);
 
 /* Number of kernels dcnv2_forward launches for this desc. */

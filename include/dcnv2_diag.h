@@ -19,6 +19,18 @@ extern "C" {
  * Returns DCNV2_ERR_DEVICE_TIMEOUT (expected) with the recorded bits in *device_code. */
 DCNV2_API dcnv2_status dcnv2_diag_timeout_selftest(uint32_t timeout_us, int32_t* device_code);
 
+/* dcnv2_forward with a CUDA event recorded on `stream` before each of its launches and one after
+ * the last: events[i] (cudaEvent_t) precedes launch i, events[dcnv2_launch_count(desc)] follows
+ * the last launch. n_events must be at least dcnv2_launch_count(desc) + 1. Used to time the
+ * kernels of one forward separately. */
+DCNV2_API dcnv2_status dcnv2_diag_forward_events(const dcnv2_desc* desc, const void* x,
+                                                 const void* offset, const void* mask,
+                                                 const void* weight, const void* bias, void* y,
+                                                 void* workspace, size_t workspace_bytes,
+                                                 float x_scale, float w_scale,
+                                                 dcnv2_stream_t stream, void* const* events,
+                                                 int32_t n_events);
+
 #ifdef __cplusplus
 }
 #endif

@@ -118,7 +118,8 @@ typedef struct {
   const float* x;      /* image base [C][H][W] (f32 values; for int8 the integer amplitudes) */
   const float* off;    /* image base [dg*2T][Ho][Wo] */
   const float* mask;   /* image base [dg*T][Ho][Wo] */
-  float* cols;
+  float* cols;         /* [C*T][np] for output pixels [p0, p0 + np) */
+  int p0, np;
 } cols_ctx;
 
 static void cols_range(void* vctx, int64_t b, int64_t e) {
@@ -133,16 +134,14 @@ static void cols_range(void* vctx, int64_t b, int64_t e) {
     const float* dhp = q->off + ((size_t)(g * 2 * T + 2 * t)) * P;
     const float* dwp = q->off + ((size_t)(g * 2 * T + 2 * t + 1)) * P;
     const float* mp = q->mask + ((size_t)(g * T + t)) * P;
-    float* out = q->cols + (size_t)ct * P;
-    for (int oh = 0; oh < q->Ho; ++oh) {
-      for (int ow = 0; ow < q->Wo; ++ow) {
-        int p = oh * q->Wo + ow;
-        /* dcn_kernel.cu:152-153: h_im = oh*stride - pad + i*dil + dh */
-        float h_im = (float)(oh * s->stride - s->padding + i * s->dilation) + dhp[p];
-        float w_im = (float)(ow * s->stride - s->padding + j * s->dilation) + dwp[p];
-        float v = mp[p] * ref_bilinear(plane, H, W, h_im, w_im);
-        out[p] = (q->mode == COLS_F16) ? round_half(v) : v;
-      }
+    float* out = q->cols + (size_t)ct * q->np;
+    for (int pi = 0; pi < q->np; ++pi) {
+      int p = q->p0 + pi, oh = p / q->Wo, ow = p % q->Wo;
+      /* dcn_kernel.cu:152-153: h_im = oh*stride - pad + i*dil + dh */
+      float h_im = (float)(oh * s->stride - s->padding + i * s->dilation) + dhp[p];
+      float w_im = (float)(ow * s->stride - s->padding + j * s->dilation) + dwp[p];
+      float v = mp[p] * ref_bilinear(plane, H, W, h_im, w_im);
+      out[pi] = (q->mode == COLS_F16) ? round_half(v) : v;
     }
   }
 }
@@ -178,36 +177,49 @@ static void gemm_range(void* vctx, int64_t b, int64_t e) {
  *           y = half(float(yh) + b)                            (dcn_plugin.cpp:148-161, :208-216)
  * Returns 0, or -1 on a bad shape / allocation failure.
  */
-int oracle_forward_ref(const oracle_shape* s, int prec, const float* x, const float* off,
-                       const float* mask, const float* w, const float* b, float* y, int threads) {
+int oracle_forward_ref_band(const oracle_shape* s, int prec, const float* x, const float* off,
+                            const float* mask, const float* w, const float* b, float* y,
+                            int threads, int p_begin, int p_end) {
   if (!s || s->n <= 0 || s->c <= 0 || s->groups <= 0 || s->c % s->groups) return -1;
   const int Ho = out_dim(s->h, s->kernel, s->stride, s->padding, s->dilation);
   const int Wo = out_dim(s->w, s->kernel, s->stride, s->padding, s->dilation);
   if (Ho <= 0 || Wo <= 0) return -1;
   const int T = s->kernel * s->kernel, P = Ho * Wo, CKK = s->c * T, O = s->out_c;
-  float* cols = (float*)malloc(sizeof(float) * (size_t)CKK * P);
-  double* acc = (double*)malloc(sizeof(double) * (size_t)O * P);
+  if (p_begin < 0 || p_end > P || p_begin >= p_end) return -1;
+  const int NP = p_end - p_begin;
+  float* cols = (float*)malloc(sizeof(float) * (size_t)CKK * NP);
+  double* acc = (double*)malloc(sizeof(double) * (size_t)O * NP);
   if (!cols || !acc) { free(cols); free(acc); return -1; }
   for (int n = 0; n < s->n; ++n) {
     cols_ctx cc = {s, prec == 1 ? COLS_F16 : COLS_F32, Ho, Wo, T,
                    x + (size_t)n * s->c * s->h * s->w, off + (size_t)n * s->groups * 2 * T * P,
-                   mask + (size_t)n * s->groups * T * P, cols};
+                   mask + (size_t)n * s->groups * T * P, cols, p_begin, NP};
     parallel_for(CKK, threads, cols_range, &cc);
-    gemm_ctx gc = {w, cols, acc, CKK, P};
+    gemm_ctx gc = {w, cols, acc, CKK, NP};
     parallel_for(O, threads, gemm_range, &gc);
-    float* yn = y + (size_t)n * O * P;
+    float* yn = y + (size_t)n * O * NP;
     for (int o = 0; o < O; ++o) {
       float bo = b ? b[o] : 0.f;
-      for (int p = 0; p < P; ++p) {
-        double a = acc[(size_t)o * P + p];
-        yn[(size_t)o * P + p] = (prec == 1) ? round_half(round_half((float)a) + bo)
-                                            : (float)(a + (double)bo);
+      for (int p = 0; p < NP; ++p) {
+        double a = acc[(size_t)o * NP + p];
+        yn[(size_t)o * NP + p] = (prec == 1) ? round_half(round_half((float)a) + bo)
+                                             : (float)(a + (double)bo);
       }
     }
   }
   free(cols);
   free(acc);
   return 0;
+}
+
+/* Whole-image form of oracle_forward_ref_band. */
+int oracle_forward_ref(const oracle_shape* s, int prec, const float* x, const float* off,
+                       const float* mask, const float* w, const float* b, float* y, int threads) {
+  if (!s) return -1;
+  const int Ho = out_dim(s->h, s->kernel, s->stride, s->padding, s->dilation);
+  const int Wo = out_dim(s->w, s->kernel, s->stride, s->padding, s->dilation);
+  if (Ho <= 0 || Wo <= 0) return -1;
+  return oracle_forward_ref_band(s, prec, x, off, mask, w, b, y, threads, 0, Ho * Wo);
 }
 
 /*
@@ -234,7 +246,7 @@ int oracle_forward_i8_ref(const oracle_shape* s, const int8_t* xq, const float* 
   for (int n = 0; n < s->n; ++n) {
     for (size_t k = 0; k < xi; ++k) xf[k] = (float)xq[(size_t)n * xi + k];
     cols_ctx cc = {s, COLS_I8REF, Ho, Wo, T, xf, off + (size_t)n * s->groups * 2 * T * P,
-                   mask + (size_t)n * s->groups * T * P, cols};
+                   mask + (size_t)n * s->groups * T * P, cols, 0, P};
     parallel_for(CKK, threads, cols_range, &cc);
     gemm_ctx gc = {wf, cols, acc, CKK, P};
     parallel_for(O, threads, gemm_range, &gc);

@@ -44,6 +44,9 @@ def lib() -> ctypes.CDLL:
         Sp = ctypes.POINTER(Shape)
         L.oracle_forward_ref.argtypes = [Sp, ctypes.c_int, fp, fp, fp, fp, fp, fp, ctypes.c_int]
         L.oracle_forward_ref.restype = ctypes.c_int
+        L.oracle_forward_ref_band.argtypes = [Sp, ctypes.c_int, fp, fp, fp, fp, fp, fp,
+                                              ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.oracle_forward_ref_band.restype = ctypes.c_int
         L.oracle_forward_i8_ref.argtypes = [Sp, i8p, fp, fp, i8p, fp, ctypes.c_float,
                                             ctypes.c_float, fp, ctypes.c_int]
         L.oracle_forward_i8_ref.restype = ctypes.c_int
@@ -96,6 +99,24 @@ def forward_ref(x, offset, mask, weight, bias, stride=1, padding=1, dilation=1, 
                                   threads or os.cpu_count() or 1)
     if rc:
         raise ValueError("oracle_forward_ref failed")
+    return y
+
+
+def forward_ref_band(x, offset, mask, weight, bias, p_begin, p_end, stride=1, padding=1,
+                     dilation=1, groups=1, precision="fp32", threads=None):
+    """Reference fast path restricted to output pixels [p_begin, p_end) of every image (the
+    bounded CPU-baseline sample). Returns y[N, O, p_end - p_begin]."""
+    x, offset, mask, weight = _f32(x), _f32(offset), _f32(mask), _f32(weight)
+    b = _f32(bias) if bias is not None else None
+    s = _shape(x, weight, stride, padding, dilation, groups)
+    y = np.empty((s.n, s.out_c, p_end - p_begin), np.float32)
+    fp = ctypes.c_float
+    rc = lib().oracle_forward_ref_band(ctypes.byref(s), 1 if precision == "fp16" else 0,
+                                       _p(x, fp), _p(offset, fp), _p(mask, fp), _p(weight, fp),
+                                       _p(b, fp) if b is not None else None, _p(y, fp),
+                                       threads or os.cpu_count() or 1, int(p_begin), int(p_end))
+    if rc:
+        raise ValueError("oracle_forward_ref_band failed")
     return y
 
 

@@ -55,11 +55,24 @@ DevInfo* device_info(int dev) {
 }
 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Optional CUDA events recorded between the launches of one forward (diagnostics only).
+struct Marks {
+  void* const* ev = nullptr;
+  int n = 0;
+  int i = 0;
+  void mark(cudaStream_t st) {
+    if (ev && i < n) cudaEventRecord(static_cast<cudaEvent_t>(ev[i++]), st);
+  }
+};
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+enum Kind { KIND_SIMT = 0, KIND_TCGEN05 = 1, KIND_F32_EXACT = 2 };
 
 struct Plan {
   int prec = 0;
-  bool fused = false;
+  int kind = KIND_SIMT;
+  bool fused = false;  // kind == KIND_TCGEN05
   int N, C, H, W, O, K, T, stride, pad, dil, dg, Ho, Wo, P, Cg;
   int elem_bytes;
   // fused-kernel configuration
@@ -67,6 +80,8 @@ struct Plan {
   int stages = 0, tiles_per_img = 0, num_tiles = 0;
   uint32_t tmem_cols = 0, a_stage_bytes = 0, b_stage_bytes = 0;
   size_t smem_bytes = 0;
+  // fp32-exact kernel configuration
+  int x_ptiles = 0, x_ctiles = 0;
   // workspace layout (offsets from the 256-byte aligned base)
   size_t off_x = 0, off_w = 0, ws_bytes = 0;
   bool tf32_single = false, precise = false;
@@ -91,10 +106,12 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
       d->stride < 1 || d->padding < 0 || d->dilation < 1 || d->deformable_groups < 1)
     return DCNV2_ERR_INVALID_ARG;
   if (d->c % d->deformable_groups) return DCNV2_ERR_INVALID_ARG;
-  if (d->math < DCNV2_MATH_DEFAULT || d->math > DCNV2_MATH_SIMT) return DCNV2_ERR_INVALID_ARG;
+  if (d->math < DCNV2_MATH_DEFAULT || d->math > DCNV2_MATH_TF32X3) return DCNV2_ERR_INVALID_ARG;
   const int prec = prec_of(d->dtype);
   if (prec < 0) return DCNV2_ERR_UNSUPPORTED;
-  if (d->math == DCNV2_MATH_TF32 && prec != PREC_F32) return DCNV2_ERR_INVALID_ARG;
+  if ((d->math == DCNV2_MATH_TF32 || d->math == DCNV2_MATH_TF32X3) && prec != PREC_F32)
+    return DCNV2_ERR_INVALID_ARG;
+  if (d->math == DCNV2_MATH_PRECISE && prec != PREC_F16) return DCNV2_ERR_INVALID_ARG;
   const int64_t ho = (int64_t(d->h) + 2 * int64_t(d->padding) -
                       int64_t(d->dilation) * (d->kernel - 1) - 1);
   const int64_t wo = (int64_t(d->w) + 2 * int64_t(d->padding) -
@@ -119,7 +136,24 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
   p.tf32_single = (d->math == DCNV2_MATH_TF32);
   p.precise = (d->math == DCNV2_MATH_PRECISE);
 
-  p.fused = (d->math != DCNV2_MATH_SIMT) && (p.Cg % chunk_elems_of(prec) == 0);
+  const bool cg_ok = p.Cg % chunk_elems_of(prec) == 0;
+  // fp32 defaults to the fp32-exact CUDA-core fused kernel; the tensor-core kinds of fp32 are
+  // opt-in (TF32, TF32X3) because their accumulation error exceeds fp32 rounding.
+  const bool f32_exact = prec == PREC_F32 && d->math == DCNV2_MATH_DEFAULT && cg_ok;
+  p.fused = (d->math != DCNV2_MATH_SIMT) && cg_ok && !f32_exact;
+  if (f32_exact) {
+    p.kind = KIND_F32_EXACT;
+    p.CBg = static_cast<int>(cdiv(p.Cg, kXK));
+    const int64_t numKB = int64_t(p.dg) * p.T * p.CBg;
+    const int64_t ptiles = cdiv(P, kXPx), ctiles = cdiv(p.O, kXCo);
+    if (numKB >= (int64_t(1) << 31) || int64_t(p.N) * ptiles * ctiles >= (int64_t(1) << 31)) {
+      p.kind = KIND_SIMT;
+    } else {
+      p.numKB = static_cast<int>(numKB);
+      p.x_ptiles = static_cast<int>(ptiles);
+      p.x_ctiles = static_cast<int>(ctiles);
+    }
+  }
   if (p.fused) {
     const int KC = block_elems_of(prec);
     const int nA = prec == PREC_F32 ? 2 : 1, nB = nA;
@@ -155,12 +189,18 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
   }
   // Workspace: [error word | x channels-last | packed weights]; +256 so that any base pointer
   // can be aligned up to 256 bytes.
+  if (p.fused) p.kind = KIND_TCGEN05;
   size_t off = kErrBytes;
-  if (p.fused) {
+  if (p.kind == KIND_TCGEN05) {
     p.off_x = off;
     off = align_up(off + size_t(p.N) * plane * p.elem_bytes, 1024);
     p.off_w = off;
     off += size_t(p.cchunks) * p.numKB * p.b_stage_bytes;
+  } else if (p.kind == KIND_F32_EXACT) {
+    p.off_x = off;
+    off = align_up(off + size_t(p.N) * plane * sizeof(float), 1024);
+    p.off_w = off;
+    off += size_t(p.x_ctiles) * p.numKB * kXK * kXCo * sizeof(float);
   }
   p.ws_bytes = align_up(off, 256) + 256;
   return DCNV2_OK;
@@ -169,7 +209,7 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
 template <int PREC>
 dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, const void* offset,
                           const void* mask, const void* weight, const void* bias, void* y,
-                          uint8_t* ws, float scale, cudaStream_t st) {
+                          uint8_t* ws, float scale, cudaStream_t st, Marks& mk) {
   using TR = PrecTraits<PREC>;
   using XT = typename TR::X;
   const uint32_t bit = 1u << PREC;
@@ -195,11 +235,13 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
       for (int n0 = 0; n0 < p.N; n0 += 65535) {
         const int nb = p.N - n0 < 65535 ? p.N - n0 : 65535;
         dim3 g2(grid.x, grid.y, static_cast<unsigned>(nb));
+        mk.mark(st);
         nchw_to_nhwc_kernel<XT><<<g2, 256, 0, st>>>(
             reinterpret_cast<const XT*>(x) + size_t(n0) * p.C * HW,
             x_nhwc + size_t(n0) * p.C * HW, p.C, HW);
       }
     } else {
+      mk.mark(st);
       nchw_to_nhwc_kernel<XT><<<grid, 256, 0, st>>>(reinterpret_cast<const XT*>(x), x_nhwc, p.C,
                                                     HW);
     }
@@ -211,6 +253,7 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
     const int64_t cap = int64_t(di->sm_count) * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
+    mk.mark(st);
     pack_weights_kernel<PREC><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
         weight, wpack, err, p.O, p.C, p.T, p.Cg, p.CBg, p.numKB, p.nrows, p.cchunks);
   }
@@ -228,14 +271,56 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
   a.scale = scale; a.precise = p.precise ? 1 : 0; a.tf32_single = p.tf32_single ? 1 : 0;
   a.timeout_ns = kDefaultTimeoutNs;
   const int grid = p.num_tiles < di->sm_count ? p.num_tiles : di->sm_count;
+  mk.mark(st);
   dcnv2_fused_kernel<PREC><<<grid, kThreads, p.smem_bytes, st>>>(a);
+  mk.mark(st);
+  return cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
+}
+
+dcnv2_status launch_f32_exact(const Plan& p, DevInfo* di, const void* x, const void* offset,
+                              const void* mask, const void* weight, const void* bias, void* y,
+                              uint8_t* ws, cudaStream_t st, Marks& mk) {
+  int* err = reinterpret_cast<int*>(ws);
+  float* x_nhwc = reinterpret_cast<float*>(ws + p.off_x);
+  float* wplain = reinterpret_cast<float*>(ws + p.off_w);
+  const int HW = p.H * p.W;
+  for (int n0 = 0; n0 < p.N; n0 += 65535) {
+    const int nb = p.N - n0 < 65535 ? p.N - n0 : 65535;
+    dim3 g(static_cast<unsigned>(cdiv(HW, 32)), static_cast<unsigned>(cdiv(p.C, 32)),
+           static_cast<unsigned>(nb));
+    mk.mark(st);
+    nchw_to_nhwc_kernel<float><<<g, 256, 0, st>>>(
+        reinterpret_cast<const float*>(x) + size_t(n0) * p.C * HW, x_nhwc + size_t(n0) * p.C * HW,
+        p.C, HW);
+  }
+  {
+    const size_t total = size_t(p.x_ctiles) * p.numKB * kXK * kXCo;
+    int64_t blocks = cdiv(static_cast<int64_t>(total), 256);
+    const int64_t cap = int64_t(di->sm_count) * 8;
+    if (blocks > cap) blocks = cap;
+    mk.mark(st);
+    pack_weights_plain_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+        reinterpret_cast<const float*>(weight), wplain, err, p.O, p.C, p.T, p.Cg, p.CBg, p.numKB,
+        p.x_ctiles);
+  }
+  ExactArgs a;
+  a.x_nhwc = x_nhwc; a.offset = reinterpret_cast<const float*>(offset);
+  a.mask = reinterpret_cast<const float*>(mask); a.wplain = wplain;
+  a.bias = reinterpret_cast<const float*>(bias); a.y = reinterpret_cast<float*>(y);
+  a.N = p.N; a.C = p.C; a.H = p.H; a.W = p.W; a.O = p.O; a.Ho = p.Ho; a.Wo = p.Wo; a.P = p.P;
+  a.K = p.K; a.T = p.T; a.stride = p.stride; a.pad = p.pad; a.dil = p.dil; a.dg = p.dg;
+  a.Cg = p.Cg; a.CBg = p.CBg; a.numKB = p.numKB; a.ptiles = p.x_ptiles; a.ctiles = p.x_ctiles;
+  const int64_t grid = int64_t(p.N) * p.x_ptiles * p.x_ctiles;
+  mk.mark(st);
+  dcnv2_f32_exact_kernel<<<static_cast<unsigned>(grid), kXThreads, 0, st>>>(a);
+  mk.mark(st);
   return cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
 }
 
 template <int PREC>
 dcnv2_status launch_simt(const Plan& p, DevInfo* di, const void* x, const void* offset,
                          const void* mask, const void* weight, const void* bias, void* y,
-                         uint8_t* ws, float scale, cudaStream_t st) {
+                         uint8_t* ws, float scale, cudaStream_t st, Marks& mk) {
   if (cudaMemsetAsync(ws, 0, sizeof(int), st) != cudaSuccess) return DCNV2_ERR_CUDA;
   SimtArgs a;
   a.x = x; a.offset = offset; a.mask = mask; a.w = weight; a.bias = bias; a.y = y;
@@ -247,7 +332,9 @@ dcnv2_status launch_simt(const Plan& p, DevInfo* di, const void* x, const void* 
   const int64_t cap = int64_t(di->sm_count) * 16;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
+  mk.mark(st);
   dcnv2_simt_kernel<PREC><<<static_cast<unsigned>(blocks), 256, 0, st>>>(a);
+  mk.mark(st);
   return cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
 }
 
@@ -302,21 +389,21 @@ size_t dcnv2_workspace_size(const dcnv2_desc* desc) {
 int32_t dcnv2_uses_tensor_cores(const dcnv2_desc* desc) {
   Plan p;
   if (make_plan(desc, &p) != DCNV2_OK) return 0;
-  return p.fused ? 1 : 0;
+  return p.kind;
 }
 
 int32_t dcnv2_launch_count(const dcnv2_desc* desc) {
   Plan p;
   if (make_plan(desc, &p) != DCNV2_OK) return 0;
-  if (!p.fused) return 1;
+  if (p.kind == KIND_SIMT) return 1;
   const int64_t zsplits = (p.N + 65534) / 65535;
   return static_cast<int32_t>(zsplits + 2);
 }
 
-dcnv2_status dcnv2_forward(const dcnv2_desc* desc, const void* x, const void* offset,
-                           const void* mask, const void* weight, const void* bias, void* y,
-                           void* workspace, size_t workspace_bytes, float x_scale, float w_scale,
-                           dcnv2_stream_t stream) {
+static dcnv2_status forward_impl(const dcnv2_desc* desc, const void* x, const void* offset,
+                                 const void* mask, const void* weight, const void* bias, void* y,
+                                 void* workspace, size_t workspace_bytes, float x_scale,
+                                 float w_scale, dcnv2_stream_t stream, Marks& mk) {
   Plan p;
   dcnv2_status s = make_plan(desc, &p);
   if (s != DCNV2_OK) return s;
@@ -340,18 +427,43 @@ dcnv2_status dcnv2_forward(const dcnv2_desc* desc, const void* x, const void* of
   if (di->major != 10) return DCNV2_ERR_NO_DEVICE;  // built for sm_100a only
   uint8_t* ws = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(workspace), 256));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (p.kind == KIND_F32_EXACT)
+    return launch_f32_exact(p, di, x, offset, mask, weight, bias, y, ws, st, mk);
   if (p.fused) {
     switch (p.prec) {
-      case PREC_F16: return launch_fused<PREC_F16>(p, di, dev, x, offset, mask, weight, bias, y, ws, scale, st);
-      case PREC_I8: return launch_fused<PREC_I8>(p, di, dev, x, offset, mask, weight, bias, y, ws, scale, st);
-      default: return launch_fused<PREC_F32>(p, di, dev, x, offset, mask, weight, bias, y, ws, scale, st);
+      case PREC_F16: return launch_fused<PREC_F16>(p, di, dev, x, offset, mask, weight, bias, y, ws, scale, st, mk);
+      case PREC_I8: return launch_fused<PREC_I8>(p, di, dev, x, offset, mask, weight, bias, y, ws, scale, st, mk);
+      default: return launch_fused<PREC_F32>(p, di, dev, x, offset, mask, weight, bias, y, ws, scale, st, mk);
     }
   }
   switch (p.prec) {
-    case PREC_F16: return launch_simt<PREC_F16>(p, di, x, offset, mask, weight, bias, y, ws, scale, st);
-    case PREC_I8: return launch_simt<PREC_I8>(p, di, x, offset, mask, weight, bias, y, ws, scale, st);
-    default: return launch_simt<PREC_F32>(p, di, x, offset, mask, weight, bias, y, ws, scale, st);
+    case PREC_F16: return launch_simt<PREC_F16>(p, di, x, offset, mask, weight, bias, y, ws, scale, st, mk);
+    case PREC_I8: return launch_simt<PREC_I8>(p, di, x, offset, mask, weight, bias, y, ws, scale, st, mk);
+    default: return launch_simt<PREC_F32>(p, di, x, offset, mask, weight, bias, y, ws, scale, st, mk);
   }
+}
+
+dcnv2_status dcnv2_forward(const dcnv2_desc* desc, const void* x, const void* offset,
+                           const void* mask, const void* weight, const void* bias, void* y,
+                           void* workspace, size_t workspace_bytes, float x_scale, float w_scale,
+                           dcnv2_stream_t stream) {
+  Marks none;
+  return forward_impl(desc, x, offset, mask, weight, bias, y, workspace, workspace_bytes, x_scale,
+                      w_scale, stream, none);
+}
+
+dcnv2_status dcnv2_diag_forward_events(const dcnv2_desc* desc, const void* x, const void* offset,
+                                       const void* mask, const void* weight, const void* bias,
+                                       void* y, void* workspace, size_t workspace_bytes,
+                                       float x_scale, float w_scale, dcnv2_stream_t stream,
+                                       void* const* events, int32_t n_events) {
+  const int32_t need = dcnv2_launch_count(desc) + 1;
+  if (!events || n_events < need || need < 2) return DCNV2_ERR_INVALID_ARG;
+  Marks mk;
+  mk.ev = events;
+  mk.n = n_events;
+  return forward_impl(desc, x, offset, mask, weight, bias, y, workspace, workspace_bytes, x_scale,
+                      w_scale, stream, mk);
 }
 
 dcnv2_status dcnv2_read_device_error(const void* workspace, dcnv2_stream_t stream,

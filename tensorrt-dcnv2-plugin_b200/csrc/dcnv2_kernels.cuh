@@ -654,6 +654,170 @@ __global__ void __launch_bounds__(256) pack_weights_kernel(const void* __restric
   }
 }
 
+// ------------------------------------------------------------------ fp32-exact fused kernel
+// The tensor-core accumulator does not add with fp32 round-to-nearest at every step, and over
+// the ~900 accumulation steps of a 3xTF32 product at C*K*K = 2304 its error reaches ~5e-5
+// relative. This kernel is the fp32-exact path: the same fused structure (samples go straight
+// to shared memory, K ordered (group, tap, 32-channel block), no column matrix in HBM), with the
+// GEMM on CUDA cores in fp32 FMA. CTA tile: 64 output pixels x 128 output channels, 256
+// threads, each accumulating 4 pixels x 8 channels; double-buffered shared-memory stages.
+constexpr int kXPx = 64, kXCo = 128, kXK = 32, kXThreads = 256;
+
+struct ExactArgs {
+  const float* x_nhwc;   // [N][H][W][C]
+  const float* offset;   // [N][dg*2*T][Ho][Wo]
+  const float* mask;     // [N][dg*T][Ho][Wo]
+  const float* wplain;   // [ctiles][numKB][32][128] (k-major rows of 128 output channels)
+  const float* bias;
+  float* y;
+  int N, C, H, W, O, Ho, Wo, P, K, T, stride, pad, dil, dg, Cg, CBg, numKB;
+  int ptiles, ctiles;
+};
+
+__global__ void __launch_bounds__(kXThreads, 2) dcnv2_f32_exact_kernel(const ExactArgs a) {
+  __shared__ __align__(16) float As[2][kXK][kXPx];
+  __shared__ __align__(16) float Bs[2][kXK][kXCo];
+  const int tid = threadIdx.x;
+  const int ct = blockIdx.x % a.ctiles;
+  const int pt = (blockIdx.x / a.ctiles) % a.ptiles;
+  const int img = blockIdx.x / (a.ctiles * a.ptiles);
+  // sampler role: pixel sp, channels sq*8 .. sq*8+7 of the 32-channel block
+  const int sp = tid & (kXPx - 1), sq = tid >> 6;
+  const int p = pt * kXPx + sp;
+  const bool pvalid = p < a.P;
+  const int pc = pvalid ? p : 0;
+  const int oh = pc / a.Wo, ow = pc - oh * a.Wo;
+  // compute role: pixels ty*4 .. +4, output channels tx*8 .. +8
+  const int ty = tid >> 4, tx = tid & 15;
+  const float* ximg = a.x_nhwc + static_cast<size_t>(img) * a.H * a.W * a.C;
+  const float* wct = a.wplain + static_cast<size_t>(ct) * a.numKB * kXK * kXCo;
+
+  float acc[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+  // prefetched state of the next K-block
+  float4 bq[4];
+  float4 xc[4][2];
+  float gw[4] = {0.f, 0.f, 0.f, 0.f};
+  int gof[4] = {0, 0, 0, 0};
+  bool cval[2];
+
+  auto prefetch = [&](int kb) {
+    const int cbg = kb % a.CBg;
+    const int t = (kb / a.CBg) % a.T;
+    const int g = kb / (a.CBg * a.T);
+    if (cbg == 0) {  // new (group, tap): new sampling geometry
+      const int ki = t / a.K, kj = t - ki * a.K;
+      float dh = 0.f, dw = 0.f, m = 0.f;
+      if (pvalid) {
+        const size_t go = (static_cast<size_t>(img) * a.dg + g) * 2 * a.T + 2 * t;
+        const size_t gm = (static_cast<size_t>(img) * a.dg + g) * a.T + t;
+        dh = __ldg(a.offset + go * a.P + p);
+        dw = __ldg(a.offset + (go + 1) * a.P + p);
+        m = __ldg(a.mask + gm * a.P + p);
+      }
+      FusedArgs ga;
+      ga.H = a.H; ga.W = a.W; ga.C = a.C;
+      const Geom gm = make_geom(ga, pvalid, oh * a.stride - a.pad + ki * a.dil,
+                                ow * a.stride - a.pad + kj * a.dil, dh, dw, m);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) { gw[c] = gm.a[c]; gof[c] = gm.off[c]; }
+    }
+    const int cig = cbg * kXK + sq * 8;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      cval[h] = (cig + 4 * h) < a.Cg;
+      const int cb = g * a.Cg + cig + 4 * h;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        xc[c][h] = cval[h] ? __ldg(reinterpret_cast<const float4*>(ximg + gof[c] + cb))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const float4* bsrc = reinterpret_cast<const float4*>(wct + static_cast<size_t>(kb) * kXK * kXCo);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) bq[i] = __ldg(bsrc + tid + i * kXThreads);
+  };
+  auto store = [&](int buf) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float* x0 = &xc[0][h].x; const float* x1 = &xc[1][h].x;
+      const float* x2 = &xc[2][h].x; const float* x3 = &xc[3][h].x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float v = __fmul_rn(gw[0], x0[e]);
+        v = __fmaf_rn(gw[1], x1[e], v);
+        v = __fmaf_rn(gw[2], x2[e], v);
+        v = __fmaf_rn(gw[3], x3[e], v);
+        As[buf][sq * 8 + 4 * h + e][sp] = cval[h] ? v : 0.f;
+      }
+    }
+    float4* bd = reinterpret_cast<float4*>(&Bs[buf][0][0]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) bd[tid + i * kXThreads] = bq[i];
+  };
+
+  prefetch(0);
+  store(0);
+  __syncthreads();
+  for (int kb = 0; kb < a.numKB; ++kb) {
+    const int buf = kb & 1;
+    const bool more = kb + 1 < a.numKB;
+    if (more) prefetch(kb + 1);
+#pragma unroll 8
+    for (int k = 0; k < kXK; ++k) {
+      const float4 av = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 8]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 8 + 4]);
+      const float ar[4] = {av.x, av.y, av.z, av.w};
+      const float br[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(ar[i], br[j], acc[i][j]);
+    }
+    if (more) store(buf ^ 1);
+    __syncthreads();
+  }
+  float* yimg = a.y + static_cast<size_t>(img) * a.O * a.P;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int o = ct * kXCo + tx * 8 + j;
+    if (o >= a.O) continue;
+    const float bo = a.bias ? __ldg(a.bias + o) : 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int pp = pt * kXPx + ty * 4 + i;
+      if (pp < a.P) yimg[static_cast<size_t>(o) * a.P + pp] = acc[i][j] + bo;
+    }
+  }
+}
+
+// Weights for the fp32-exact kernel: [ctile][kb][k][128 co], zero padded.
+__global__ void __launch_bounds__(256) pack_weights_plain_kernel(const float* __restrict__ w,
+                                                                 float* __restrict__ wp, int* err,
+                                                                 int O, int C, int T, int Cg,
+                                                                 int CBg, int numKB, int ctiles) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) *err = 0;
+  const size_t total = static_cast<size_t>(ctiles) * numKB * kXK * kXCo;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int co = static_cast<int>(idx % kXCo);
+    const int k = static_cast<int>((idx / kXCo) % kXK);
+    const size_t blk = idx / (static_cast<size_t>(kXCo) * kXK);
+    const int kb = static_cast<int>(blk % numKB);
+    const int ct = static_cast<int>(blk / numKB);
+    const int cbg = kb % CBg, t = (kb / CBg) % T, g = kb / (CBg * T);
+    const int o = ct * kXCo + co;
+    const int cig = cbg * kXK + k;
+    float v = 0.f;
+    if (o < O && cig < Cg) v = w[(static_cast<size_t>(o) * C + g * Cg + cig) * T + t];
+    wp[idx] = v;
+  }
+}
+
 // ------------------------------------------------------------------ CUDA-core fallback
 // One thread per output element, any shape (the reference's naive kernel structure,
 // src/dcn_kernel.cu:33-65, extended to N, groups and the int8 requantisation). Column values use

@@ -37,6 +37,7 @@ class Math(enum.IntEnum):
     PRECISE = 1
     TF32 = 2
     SIMT = 3
+    TF32X3 = 4
 
 
 FORMAT_LINEAR = 0
@@ -98,6 +99,9 @@ def _load() -> ctypes.CDLL:
                                                   ctypes.POINTER(P), P, ctypes.c_size_t, P]),
         "dcnv2_diag_timeout_selftest": (ctypes.c_int, [ctypes.c_uint32,
                                                        ctypes.POINTER(ctypes.c_int32)]),
+        "dcnv2_diag_forward_events": (ctypes.c_int, [Dp, P, P, P, P, P, P, P, ctypes.c_size_t,
+                                                     ctypes.c_float, ctypes.c_float, P,
+                                                     ctypes.POINTER(P), ctypes.c_int32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -116,7 +120,7 @@ EXPORTED = (
     "dcnv2_plugin_create", "dcnv2_plugin_clone", "dcnv2_plugin_destroy",
     "dcnv2_plugin_serialize", "dcnv2_plugin_nb_outputs", "dcnv2_plugin_output_dtype",
     "dcnv2_plugin_output_shape", "dcnv2_plugin_supports_format", "dcnv2_plugin_workspace_size",
-    "dcnv2_plugin_enqueue", "dcnv2_diag_timeout_selftest",
+    "dcnv2_plugin_enqueue", "dcnv2_diag_timeout_selftest", "dcnv2_diag_forward_events",
 )
 
 
@@ -138,8 +142,9 @@ def workspace_size(desc: Desc) -> int:
     return int(lib.dcnv2_workspace_size(ctypes.byref(desc)))
 
 
-def uses_tensor_cores(desc: Desc) -> bool:
-    return bool(lib.dcnv2_uses_tensor_cores(ctypes.byref(desc)))
+def uses_tensor_cores(desc: Desc) -> int:
+    """1 = fused tcgen05 kernel, 2 = fused fp32-exact CUDA-core kernel, 0 = per-output kernel."""
+    return int(lib.dcnv2_uses_tensor_cores(ctypes.byref(desc)))
 
 
 def launch_count(desc: Desc) -> int:
@@ -169,3 +174,12 @@ def timeout_selftest(timeout_us: int):
     code = ctypes.c_int32(0)
     st = lib.dcnv2_diag_timeout_selftest(int(timeout_us), ctypes.byref(code))
     return int(st), int(code.value)
+
+
+def forward_events_raw(desc: Desc, x, offset, mask, weight, bias, y, workspace, workspace_bytes,
+                       x_scale, w_scale, stream, events) -> int:
+    """dcnv2_forward with cudaEvent_t handles (ints) recorded around each launch."""
+    arr = (ctypes.c_void_p * len(events))(*[int(e) for e in events])
+    return int(lib.dcnv2_diag_forward_events(ctypes.byref(desc), x, offset, mask, weight, bias,
+                                             y, workspace, workspace_bytes, float(x_scale),
+                                             float(w_scale), stream, arr, len(events)))

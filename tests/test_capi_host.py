@@ -123,7 +123,7 @@ def test_workspace_rule():
 @pytest.mark.parametrize("kw", [
     dict(n=0), dict(c=0), dict(h=0), dict(out_c=0), dict(kernel=0), dict(stride=0),
     dict(padding=-1), dict(dilation=0), dict(deformable_groups=0), dict(deformable_groups=3),
-    dict(h=1, w=1, padding=0), dict(math=9),
+    dict(h=1, w=1, padding=0), dict(math=9), dict(math=-1),
 ])
 def test_invalid_descs(kw):
     base = dict(n=1, c=16, h=8, w=8, out_c=8)
@@ -154,11 +154,16 @@ def test_forward_argument_errors_before_any_launch():
 
 def test_math_modes_select_kernels():
     f32 = capi.make_desc(1, 256, 64, 64, 256, dtype=DType.FLOAT)
-    assert capi.uses_tensor_cores(f32)
+    assert capi.uses_tensor_cores(f32) == 2  # fp32-exact fused CUDA-core kernel
+    assert capi.launch_count(f32) == 3
+    for m in (Math.TF32, Math.TF32X3):
+        assert capi.uses_tensor_cores(capi.make_desc(1, 256, 64, 64, 256, dtype=DType.FLOAT,
+                                                     math=m)) == 1
     simt = capi.make_desc(1, 256, 64, 64, 256, dtype=DType.FLOAT, math=Math.SIMT)
     assert not capi.uses_tensor_cores(simt)
-    tf32_on_half = capi.make_desc(1, 256, 64, 64, 256, dtype=DType.HALF, math=Math.TF32)
-    assert capi.workspace_size(tf32_on_half) == 0
+    for bad in ((DType.HALF, Math.TF32), (DType.INT8, Math.TF32X3), (DType.FLOAT, Math.PRECISE)):
+        d = capi.make_desc(1, 256, 64, 64, 256, dtype=bad[0], math=bad[1])
+        assert capi.workspace_size(d) == 0
     # int8 needs 16-channel groups for the tensor-core path
     assert capi.uses_tensor_cores(capi.make_desc(1, 32, 8, 8, 8, dtype=DType.INT8))
     assert not capi.uses_tensor_cores(capi.make_desc(1, 24, 8, 8, 8, dtype=DType.INT8))

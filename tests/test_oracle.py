@@ -116,3 +116,13 @@ def test_int8_reference_path_tolerance(golden_dir):
     y = oracle.forward_i8_ref(xq, fx["offset"], fx["mask"], wq, fx["bias"], xs, ws)
     rel = np.abs(y - fx["y"]).sum() / np.abs(fx["y"]).sum()
     assert rel < 0.1  # src/test_dcn_int8_gemm.cu:89 (README reports 1.27%)
+
+
+def test_band_matches_full(golden_dir):
+    fx = load(golden_dir, "tv_n2_dg2_s2.npz")
+    full = run_ref(fx)
+    ho, wo = full.shape[2:]
+    band = oracle.forward_ref_band(fx["x"], fx["offset"], fx["mask"], fx["weight"], fx["bias"],
+                                   5, 23, fx["stride"], fx["padding"], fx["dilation"],
+                                   fx["groups"])
+    assert np.array_equal(band, full.reshape(full.shape[0], full.shape[1], -1)[:, :, 5:23])
