@@ -56,7 +56,8 @@ typedef enum {
   DCNV2_ERR_WORKSPACE = 3,     /* workspace pointer null or smaller than dcnv2_workspace_size */
   DCNV2_ERR_CUDA = 4,          /* a CUDA runtime call or kernel launch failed */
   DCNV2_ERR_NO_DEVICE = 5,     /* no usable sm_100 device for the current context */
-  DCNV2_ERR_DEVICE_TIMEOUT = 6 /* a kernel gave up waiting on an on-chip barrier (see error word) */
+  DCNV2_ERR_DEVICE_TIMEOUT = 6, /* a kernel gave up waiting on an on-chip barrier (error word) */
+  DCNV2_ERR_SCRATCH_LIMIT = 7   /* problem needs more than DCNV2_STATIC_SCRATCH_BYTES of scratch */
 } dcnv2_status;
 
 /* Math modes (dcnv2_desc.math). */
@@ -100,6 +101,32 @@ DCNV2_API dcnv2_status dcnv2_forward(const dcnv2_desc* desc,
                            const void* weight, const void* bias, void* y,
                            void* workspace, size_t workspace_bytes,
                            float x_scale, float w_scale, dcnv2_stream_t stream);
+
+/* Size of the library's built-in static scratch buffer used by dcnv2_forward_static_scratch. */
+#define DCNV2_STATIC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/* dcnv2_forward for callers that cannot allocate device memory: no counterpart in the reference
+ * plugin (there TensorRT always hands enqueue a workspace). Some callers must not call cudaMalloc
+ * once they run: an engine whose memory plan is fixed at build time, a serving loop where an
+ * allocation would synchronise the device and stall other streams, or a process held to a fixed
+ * device-memory budget by its own pool. This entry point takes only inputs and outputs; its
+ * scratch (the channels-last copy of x, the packed weights and the error word) lives in one
+ * file-scope static __device__ buffer of DCNV2_STATIC_SCRATCH_BYTES (32 MiB) that every GPU which
+ * loads the library holds until the process exits. It calls no cudaMalloc, cudaFree or other
+ * allocating routine.
+ *   - Problems whose scratch need (dcnv2_workspace_size) exceeds the buffer are rejected with
+ *     DCNV2_ERR_SCRATCH_LIMIT before anything is launched.
+ *   - The first call on each device looks up the buffer's device address (cudaGetSymbolAddress
+ *     with that device current); make that first call before any stream capture begins.
+ *   - All calls on a device share the one buffer and it keeps the last call's contents (each call
+ *     rewrites every byte it reads and clears the error word itself). Calls that overlap on the
+ *     GPU — on different streams, or from different host threads — race on it; issue them on one
+ *     stream, one after another. */
+DCNV2_API dcnv2_status dcnv2_forward_static_scratch(const dcnv2_desc* desc, const void* x,
+                                                   const void* offset, const void* mask,
+                                                   const void* weight, const void* bias, void* y,
+                                                   float x_scale, float w_scale,
+                                                   dcnv2_stream_t stream);
 
 /* Copies the device error word of the last forward that used `workspace` to *code (0 = none;
  * otherwise DCNV2_DEVERR_* bits) after synchronising `stream`. Test and debug helper. */

@@ -491,6 +491,8 @@ const char* dcnv2_status_string(dcnv2_status status) {
     case DCNV2_ERR_CUDA: return "CUDA runtime error";
     case DCNV2_ERR_NO_DEVICE: return "no sm_100 device";
     case DCNV2_ERR_DEVICE_TIMEOUT: return "kernel barrier wait timed out";
+    case DCNV2_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the 32 MiB static buffer holds";
   }
   return "unknown status";
 }
@@ -519,3 +521,55 @@ dcnv2_status dcnv2_diag_timeout_selftest(uint32_t timeout_us, int32_t* device_co
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free forward. Some callers cannot call cudaMalloc while they run (a fixed memory
+// plan, a latency-critical loop where an allocation would synchronise the device, a hard device
+// memory budget), so they cannot provide the workspace dcnv2_forward needs. For them the scratch
+// lives here, in one file-scope buffer that every GPU which loads this library holds until the
+// process exits. Host code must not pass `dcnv2_static_scratch` itself to a kernel — in host code
+// that name is only a stand-in for the device symbol — so its device address is looked up once
+// per device with cudaGetSymbolAddress and cached. The forward that runs is dcnv2_forward,
+// unchanged, with this buffer as its workspace; it rewrites every scratch byte it reads and its
+// weight-pack launch (or the memset of the CUDA-core path) clears the error word, so nothing
+// carries over from the previous call. Concurrent calls on one device race on the buffer.
+static __device__ __align__(256) unsigned char dcnv2_static_scratch[DCNV2_STATIC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_static_scratch_mu;
+void* g_static_scratch_addr[dcnv2::kMaxDevices] = {};
+}  // namespace
+
+extern "C" dcnv2_status dcnv2_forward_static_scratch(const dcnv2_desc* desc, const void* x,
+                                                     const void* offset, const void* mask,
+                                                     const void* weight, const void* bias,
+                                                     void* y, float x_scale, float w_scale,
+                                                     dcnv2_stream_t stream) {
+  Plan p;
+  const dcnv2_status s = make_plan(desc, &p);
+  if (s != DCNV2_OK) return s;
+  if (p.ws_bytes > DCNV2_STATIC_SCRATCH_BYTES) return DCNV2_ERR_SCRATCH_LIMIT;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return DCNV2_ERR_NO_DEVICE;
+  }
+  if (dev < 0 || dev >= dcnv2::kMaxDevices) return DCNV2_ERR_NO_DEVICE;
+  void* scratch = nullptr;
+  {
+    // Once per device, with that device current: the device address of the static buffer.
+    std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+    if (!g_static_scratch_addr[dev]) {
+      void* addr = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&addr, dcnv2_static_scratch);
+      if (e != cudaSuccess || !addr) {
+        cudaGetLastError();
+        return DCNV2_ERR_CUDA;
+      }
+      g_static_scratch_addr[dev] = addr;
+    }
+    scratch = g_static_scratch_addr[dev];
+  }
+  return dcnv2_forward(desc, x, offset, mask, weight, bias, y, scratch,
+                       DCNV2_STATIC_SCRATCH_BYTES, x_scale, w_scale, stream);
+}

@@ -23,6 +23,11 @@ class Status(enum.IntEnum):
     ERR_CUDA = 4
     ERR_NO_DEVICE = 5
     ERR_DEVICE_TIMEOUT = 6
+    ERR_SCRATCH_LIMIT = 7
+
+
+#: Size of the library's static scratch buffer (DCNV2_STATIC_SCRATCH_BYTES in include/dcnv2.h).
+STATIC_SCRATCH_BYTES = 32 * 1024 * 1024
 
 
 class DType(enum.IntEnum):
@@ -72,6 +77,8 @@ def _load() -> ctypes.CDLL:
         "dcnv2_workspace_size": (ctypes.c_size_t, [Dp]),
         "dcnv2_forward": (ctypes.c_int, [Dp, P, P, P, P, P, P, P, ctypes.c_size_t, ctypes.c_float,
                                          ctypes.c_float, P]),
+        "dcnv2_forward_static_scratch": (ctypes.c_int, [Dp, P, P, P, P, P, P, ctypes.c_float,
+                                                        ctypes.c_float, P]),
         "dcnv2_read_device_error": (ctypes.c_int, [P, P, ctypes.POINTER(ctypes.c_int32)]),
         "dcnv2_uses_tensor_cores": (ctypes.c_int32, [Dp]),
         "dcnv2_launch_count": (ctypes.c_int32, [Dp]),
@@ -114,7 +121,8 @@ lib = _load()
 
 #: Every entry point include/dcnv2.h and include/dcnv2_diag.h declare.
 EXPORTED = (
-    "dcnv2_output_shape", "dcnv2_workspace_size", "dcnv2_forward", "dcnv2_read_device_error",
+    "dcnv2_output_shape", "dcnv2_workspace_size", "dcnv2_forward",
+    "dcnv2_forward_static_scratch", "dcnv2_read_device_error",
     "dcnv2_uses_tensor_cores", "dcnv2_launch_count", "dcnv2_status_string", "dcnv2_plugin_name",
     "dcnv2_plugin_version", "dcnv2_plugin_namespace", "dcnv2_plugin_field_names",
     "dcnv2_plugin_create", "dcnv2_plugin_clone", "dcnv2_plugin_destroy",
@@ -183,3 +191,10 @@ def forward_events_raw(desc: Desc, x, offset, mask, weight, bias, y, workspace, 
     return int(lib.dcnv2_diag_forward_events(ctypes.byref(desc), x, offset, mask, weight, bias,
                                              y, workspace, workspace_bytes, float(x_scale),
                                              float(w_scale), stream, arr, len(events)))
+
+
+def forward_static_scratch_raw(desc: Desc, x, offset, mask, weight, bias, y, x_scale=1.0,
+                               w_scale=1.0, stream=0) -> int:
+    """Raw call of the allocation-free forward (scratch in the library's static buffer)."""
+    return int(lib.dcnv2_forward_static_scratch(ctypes.byref(desc), x, offset, mask, weight, bias,
+                                                y, float(x_scale), float(w_scale), stream))
