@@ -17,6 +17,7 @@
 
 #include "../../include/dcnv2.h"
 #include "../../include/dcnv2_diag.h"
+#include <cudaTypedefs.h>
 #include "dcnv2_kernels.cuh"
 
 namespace dcnv2 {
@@ -56,6 +57,22 @@ DevInfo* device_info(int dev) {
 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link needed).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
 // Optional CUDA events recorded between the launches of one forward (diagnostics only).
 struct Marks {
   void* const* ev = nullptr;
@@ -84,6 +101,10 @@ struct Plan {
   int x_ptiles = 0, x_ctiles = 0;
   // workspace layout (offsets from the 256-byte aligned base)
   size_t off_x = 0, off_w = 0, ws_bytes = 0;
+  // shared-memory window of x for the fused kernel (two buffers of win_bytes)
+  bool use_win = false;
+  int win_rows = 0, win_top = 0;
+  uint32_t win_bytes = 0;
   bool tf32_single = false, precise = false;
 };
 
@@ -185,6 +206,36 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
       p.tiles_per_img = static_cast<int>(tiles_per_img);
       p.num_tiles = static_cast<int>(num_tiles);
       p.smem_bytes = fixed + size_t(stages) * per_stage;
+      // Window of x: whole rows (W <= 256, one TMA box) covering every tap of every pixel of a
+      // tile whose offsets lie in (-1 - M, 1 + M), for the largest margin M <= 2 that still
+      // leaves two pipeline stages. Corners outside it are read from global memory.
+      if (p.W <= 256) {
+        int rows_max = 0;
+        const int64_t loop = tiles_per_img < 4096 ? tiles_per_img : 4096;
+        for (int64_t pt = 0; pt < loop; ++pt) {
+          const int64_t a0 = pt * kTileM, a1 = (a0 + kTileM < P ? a0 + kTileM : P) - 1;
+          const int rows = static_cast<int>(a1 / p.Wo - a0 / p.Wo + 1);
+          if (rows > rows_max) rows_max = rows;
+        }
+        if (tiles_per_img > 4096 && p.Wo > 4096) rows_max = 1 << 20;  // no exact bound: no window
+        const int64_t base = int64_t(rows_max - 1) * p.stride + int64_t(p.K - 1) * p.dil + 3;
+        for (int M = 2; M >= 0; --M) {
+          const int64_t rows = base + 2 * M;
+          if (rows > 256) continue;
+          const size_t wb = size_t(rows) * p.W * kRowBytes;
+          // window byte offsets travel in 16 bits; two stages at least
+          if (wb > 65536 || 2 * wb + fixed + 2 * per_stage > kSmemLimit) continue;
+          int sw = static_cast<int>((kSmemLimit - fixed - 2 * wb) / per_stage);
+          if (sw > kMaxStages) sw = kMaxStages;
+          p.use_win = true;
+          p.win_rows = static_cast<int>(rows);
+          p.win_top = p.pad + 1 + M;
+          p.win_bytes = static_cast<uint32_t>(wb);
+          p.stages = sw;
+          p.smem_bytes = fixed + size_t(sw) * per_stage + 2 * wb;
+          break;
+        }
+      }
     }
   }
   // Workspace: [error word | x channels-last | packed weights]; +256 so that any base pointer
@@ -214,8 +265,13 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
   using XT = typename TR::X;
   const uint32_t bit = 1u << PREC;
   if (!(di->attr_set.load(std::memory_order_acquire) & bit)) {
-    if (cudaFuncSetAttribute(dcnv2_fused_kernel<PREC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemLimit)) != cudaSuccess)
+    const int lim = static_cast<int>(kSmemLimit);
+    const cudaFuncAttribute at = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    if (cudaFuncSetAttribute(dcnv2_fused_kernel<PREC, false, 9>, at, lim) != cudaSuccess ||
+        cudaFuncSetAttribute(dcnv2_fused_kernel<PREC, false, 0>, at, lim) != cudaSuccess ||
+        (PREC == PREC_F16 &&
+         (cudaFuncSetAttribute(dcnv2_fused_kernel<PREC, true, 9>, at, lim) != cudaSuccess ||
+          cudaFuncSetAttribute(dcnv2_fused_kernel<PREC, true, 0>, at, lim) != cudaSuccess)))
       return DCNV2_ERR_CUDA;
     di->attr_set.fetch_or(bit, std::memory_order_acq_rel);
   }
@@ -270,9 +326,38 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
   a.a_stage_bytes = p.a_stage_bytes; a.b_stage_bytes = p.b_stage_bytes;
   a.scale = scale; a.precise = p.precise ? 1 : 0; a.tf32_single = p.tf32_single ? 1 : 0;
   a.timeout_ns = kDefaultTimeoutNs;
+  a.use_win = 0; a.win_rows = p.win_rows; a.win_top = p.win_top; a.win_bytes = p.win_bytes;
+  CUtensorMap tmap;
+  std::memset(&tmap, 0, sizeof(tmap));
+  if (p.use_win) {
+    // x channels-last seen as bytes: dims {C*EB, W, H, N}; box = one 128-byte channel block of
+    // win_rows whole rows of one image.
+    const cuuint64_t eb = static_cast<cuuint64_t>(p.elem_bytes);
+    const cuuint64_t dims[4] = {cuuint64_t(p.C) * eb, cuuint64_t(p.W), cuuint64_t(p.H),
+                                cuuint64_t(p.N)};
+    const cuuint64_t strides[3] = {cuuint64_t(p.C) * eb, cuuint64_t(p.W) * p.C * eb,
+                                   cuuint64_t(p.H) * p.W * p.C * eb};
+    const cuuint32_t box[4] = {static_cast<cuuint32_t>(kRowBytes), static_cast<cuuint32_t>(p.W),
+                               static_cast<cuuint32_t>(p.win_rows), 1u};
+    const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (encode && encode(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, x_nhwc, dims, strides, box,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+      a.use_win = 1;  // otherwise every corner is read from global memory
+  }
   const int grid = p.num_tiles < di->sm_count ? p.num_tiles : di->sm_count;
   mk.mark(st);
-  dcnv2_fused_kernel<PREC><<<grid, kThreads, p.smem_bytes, st>>>(a);
+  // 3x3 kernels take the variant with the nine taps unrolled
+  const bool k3 = p.T == 9;
+  if (PREC == PREC_F16 && p.precise) {
+    if (k3) dcnv2_fused_kernel<PREC, true, 9><<<grid, kThreads, p.smem_bytes, st>>>(a, tmap);
+    else dcnv2_fused_kernel<PREC, true, 0><<<grid, kThreads, p.smem_bytes, st>>>(a, tmap);
+  } else {
+    if (k3) dcnv2_fused_kernel<PREC, false, 9><<<grid, kThreads, p.smem_bytes, st>>>(a, tmap);
+    else dcnv2_fused_kernel<PREC, false, 0><<<grid, kThreads, p.smem_bytes, st>>>(a, tmap);
+  }
   mk.mark(st);
   return cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
 }

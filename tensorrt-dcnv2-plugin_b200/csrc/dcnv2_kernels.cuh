@@ -10,15 +10,17 @@
 //   warp 1       MMA issuer: tcgen05.mma (kind::f16 / kind::i8 / kind::tf32) into TMEM,
 //                accumulator double-buffered so the epilogue overlaps the next tile
 //   warps 2-5    epilogue: tcgen05.ld from TMEM, + bias (x x_scale*w_scale for int8), store y
-//   warps 6-13   samplers: bilinear x mask samples of 128 output pixels x one K-block, written
+//   warps 6-21   samplers: bilinear x mask samples of 128 output pixels x one K-block, written
 //                straight into the A-operand tile (one 16-byte chunk of channels per thread)
 //
 // GEMM view per tile: D[128 pixels, O] = A[128 pixels, C*K*K] * B[O, C*K*K]^T. K is ordered
-// (deformable group g, tap t, channel block) so that one K-block shares one sampling geometry;
-// the corner weights of a (pixel, tap, group) are computed once and reused for every channel
-// block of that group. x is read channels-last (a pre-pass transposes NCHW -> NHWC), so every
-// corner fetch is a 16-byte vector of 8 fp16 / 16 int8 / 4 fp32 channels.
+// (deformable group g, channel block, tap t): one K-block has one sampling geometry per pixel,
+// and the K*K consecutive K-blocks of a channel block read one shared-memory window of x (a
+// TMA box of whole rows of the channels-last copy, double-buffered), so most corner fetches are
+// 16-byte shared-memory loads of 8 fp16 / 16 int8 / 4 fp32 channels. The corner weights of a
+// (pixel, tap, group) are computed once per tile and reused for every channel block.
 #pragma once
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -38,10 +40,11 @@ constexpr int kMmaWarp = 1;
 constexpr int kEpiWarp0 = 2;
 constexpr int kNumEpiWarps = 4;
 constexpr int kSampWarp0 = kEpiWarp0 + kNumEpiWarps;
-constexpr int kNumSampWarps = 8;
-constexpr int kThreads = (kSampWarp0 + kNumSampWarps) * 32;  // 448
+constexpr int kNumSampWarps = 16;
+constexpr int kThreads = (kSampWarp0 + kNumSampWarps) * 32;  // 704
 constexpr int kMaxStages = 8;
-constexpr int kRowsPerSampThread = kTileM * 8 / (kNumSampWarps * 32);  // 4
+constexpr int kRowsPerSampThread = kTileM * 8 / (kNumSampWarps * 32);  // 2
+constexpr int kSampRowStride = kNumSampWarps * 32 / 8;              // 64
 
 template <int P> struct PrecTraits;
 template <> struct PrecTraits<PREC_F16> {
@@ -82,22 +85,36 @@ struct FusedArgs {
   uint32_t tmem_cols;
   uint32_t a_stage_bytes, b_stage_bytes;
   float scale;             // int8: x_scale * w_scale
+  int use_win;             // 1: corners come from a shared-memory window of x (TMA)
+  int win_rows;            // rows of x in one window (all W columns, 128 bytes per pixel)
+  int win_top;             // window top row = first output row of the tile * stride - win_top
+  uint32_t win_bytes;      // win_rows * W * 128
   int precise;             // fp16: fp32 sampler arithmetic
   int tf32_single;         // fp32: hi*hi only (plain TF32)
   unsigned long long timeout_ns;
 };
 
 // ------------------------------------------------------------------ bounded mbarrier wait
-// Spins on the barrier; gives up after timeout_ns (sets the CTA abort flag and the device
-// error word) or as soon as another role of this CTA has aborted.
+// Waits for the phase of `bar` with the given parity. Gives up after timeout_ns (sets the CTA
+// abort flag and the device error word) or as soon as another role of this CTA has aborted;
+// both are checked every 16 tries so that a waiting warp issues few instructions.
+// SLEEP_NS > 0 adds a nanosleep between tries; SLEEP_NS < 0 (kSuspend) lets the hardware suspend
+// the thread until the phase completes; 0 spins (the MMA issuer, whose wake-up latency is on the
+// critical path). Waiting warps that do not spin leave the issue slots to the working ones.
+constexpr int kSuspend = -1;
+template <int SLEEP_NS = 0>
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const FusedArgs& a,
                                          volatile int* abort_flag, int code) {
   if (ptx::mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = ptx::global_timer_ns();
-  uint32_t n = 0;
-  while (true) {
-    if (ptx::mbar_try_wait(bar, parity)) return true;
-    if ((++n & 31u) == 0) {
+  for (uint32_t n = 1;; ++n) {
+    if constexpr (SLEEP_NS > 0) __nanosleep(static_cast<unsigned>(SLEEP_NS));
+    if constexpr (SLEEP_NS < 0) {
+      if (ptx::mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
+    } else {
+      if (ptx::mbar_try_wait(bar, parity)) return true;
+    }
+    if ((n & 15u) == 0) {
       if (*abort_flag) return false;
       if (ptx::global_timer_ns() - t0 > a.timeout_ns) {
         *abort_flag = 1;
@@ -153,6 +170,28 @@ __device__ __forceinline__ Geom make_geom(const FusedArgs& a, bool valid, int ba
   return g;
 }
 
+// Corner c of make_geom alone (0: (h0,w0), 1: (h0,w0+1), 2: (h0+1,w0), 3: (h0+1,w0+1)), with
+// the same operations in the same order, so weight and offset are bit-identical to make_geom's.
+__device__ __forceinline__ void make_corner(const FusedArgs& a, bool valid, int base_h,
+                                            int base_w, float dh, float dw, float m, int c,
+                                            float& wt, int& off) {
+  const float hf = __fadd_rn(static_cast<float>(base_h), dh);
+  const float wf = __fadd_rn(static_cast<float>(base_w), dw);
+  const bool inside = valid && !(hf <= -1.f || hf >= static_cast<float>(a.H) || wf <= -1.f ||
+                                 wf >= static_cast<float>(a.W));
+  const float h0f = floorf(hf), w0f = floorf(wf);
+  const int h0 = inside ? static_cast<int>(h0f) : 0;
+  const int w0 = inside ? static_cast<int>(w0f) : 0;
+  const float lh = __fsub_rn(hf, h0f), lw = __fsub_rn(wf, w0f);
+  const float hh = __fsub_rn(1.f, lh), hw = __fsub_rn(1.f, lw);
+  const int dy = c >> 1, dx = c & 1;
+  const float fy = dy ? lh : hh, fx = dx ? lw : hw;
+  const int hc = h0 + dy, wc = w0 + dx;
+  const bool ok = inside && hc >= 0 && hc <= a.H - 1 && wc >= 0 && wc <= a.W - 1;
+  wt = ok ? __fmul_rn(m, __fmul_rn(fy, fx)) : 0.f;
+  off = (min(max(hc, 0), a.H - 1) * a.W + min(max(wc, 0), a.W - 1)) * a.C;
+}
+
 __device__ __forceinline__ float load_geom_value(const __half* p) { return __half2float(*p); }
 __device__ __forceinline__ float load_geom_value(const float* p) { return __ldg(p); }
 
@@ -172,6 +211,16 @@ __device__ __forceinline__ uint32_t f16_mix_fast(uint32_t a0, uint32_t a1, uint3
   v = __hfma2(bits_h2(a1), bits_h2(x1), v);
   v = __hfma2(bits_h2(a2), bits_h2(x2), v);
   v = __hfma2(bits_h2(a3), bits_h2(x3), v);
+  return h2_bits(v);
+}
+// Same mix with the (duplicated) fp16 weights as __half2 operands.
+__device__ __forceinline__ uint32_t f16_mix_h2(__half2 a0, __half2 a1, __half2 a2, __half2 a3,
+                                               uint32_t x0, uint32_t x1, uint32_t x2,
+                                               uint32_t x3) {
+  __half2 v = __hmul2(a0, bits_h2(x0));
+  v = __hfma2(a1, bits_h2(x1), v);
+  v = __hfma2(a2, bits_h2(x2), v);
+  v = __hfma2(a3, bits_h2(x3), v);
   return h2_bits(v);
 }
 // fp16 precise path: fp32 arithmetic, one rounding to fp16 per column value.
@@ -225,8 +274,9 @@ __device__ __forceinline__ void f32_mix(const float (&a)[4], const uint4& x0, co
 }
 
 // ------------------------------------------------------------------ the fused kernel
-template <int PREC>
-__global__ void __launch_bounds__(kThreads, 1) dcnv2_fused_kernel(const FusedArgs args) {
+template <int PREC, bool PRECISE, int KT>
+__global__ void __launch_bounds__(kThreads, 1)
+    dcnv2_fused_kernel(const FusedArgs args, const __grid_constant__ CUtensorMap tmap_x) {
   using TR = PrecTraits<PREC>;
   using GT = typename TR::G;
   using YT = typename TR::Y;
@@ -237,14 +287,17 @@ __global__ void __launch_bounds__(kThreads, 1) dcnv2_fused_kernel(const FusedArg
   const int S = args.stages;
   uint8_t* a_smem = smem;
   uint8_t* b_smem = smem + S * args.a_stage_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(b_smem + S * args.b_stage_bytes);
+  uint8_t* w_smem = b_smem + S * args.b_stage_bytes;       // 2 x-window buffers (if used)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(w_smem + (args.use_win ? 2 * args.win_bytes : 0));
   const uint32_t full_a = ptx::smem_addr(bars);          // [S]
   const uint32_t full_b = full_a + 8 * S;                // [S]
   const uint32_t empty = full_b + 8 * S;                 // [S]
   const uint32_t tfull = empty + 8 * S;                  // [2]
   const uint32_t tempty = tfull + 16;                    // [2]
   const uint32_t drain = tempty + 16;                    // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 5);
+  const uint32_t win_full = drain + 8;                   // [2]
+  const uint32_t win_empty = win_full + 16;              // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   if (threadIdx.x == 0) {
@@ -258,6 +311,10 @@ __global__ void __launch_bounds__(kThreads, 1) dcnv2_fused_kernel(const FusedArg
       ptx::mbar_init(tempty + 8 * i, kNumEpiWarps);
     }
     ptx::mbar_init(drain, 1);
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(win_full + 8 * i, 1);
+      ptx::mbar_init(win_empty + 8 * i, kNumSampWarps);
+    }
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -273,7 +330,8 @@ __global__ void __launch_bounds__(kThreads, 1) dcnv2_fused_kernel(const FusedArg
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer (weights)
     if (lane == 0) {
-      int it = 0;
+      int it = 0, s = 0;
+      uint32_t ph = 0;
       bool ok = true;
       const uint32_t b_base = ptx::smem_addr(b_smem);
       for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
@@ -281,9 +339,8 @@ __global__ void __launch_bounds__(kThreads, 1) dcnv2_fused_kernel(const FusedArg
         decode_tile(args, tile, img, pt, cc);
         const uint8_t* src = args.wpack + static_cast<size_t>(cc) * args.numKB * args.b_stage_bytes;
         for (int kb = 0; kb < args.numKB; ++kb, ++it) {
-          const int s = it % S;
-          const uint32_t ph = (it / S) & 1;
-          if (!wait_bar(empty + 8 * s, ph ^ 1, args, abort_flag, DCNV2_DEVERR_TIMEOUT_PRODUCER)) {
+          if (!wait_bar<kSuspend>(empty + 8 * s, ph ^ 1, args, abort_flag,
+                                  DCNV2_DEVERR_TIMEOUT_PRODUCER)) {
             ok = false;
             break;
           }
@@ -291,6 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcnv2_fused_kernel(const FusedArg
           ptx::bulk_copy_g2s(b_base + s * args.b_stage_bytes,
                              src + static_cast<size_t>(kb) * args.b_stage_bytes,
                              args.b_stage_bytes, full_b + 8 * s);
+          if (++s == S) { s = 0; ph ^= 1u; }
         }
       }
       // Wait for the copies still in flight (at most the last one per stage) before the CTA
@@ -303,44 +361,46 @@ __global__ void __launch_bounds__(kThreads, 1) dcnv2_fused_kernel(const FusedArg
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
+    // A single thread on the critical path: it spins (the samplers suspend), keeps stage and
+    // phase counters incrementally and only patches the start-address field of the descriptors.
     if (lane == 0) {
       uint32_t idesc;
       if (PREC == PREC_F16) idesc = ptx::make_idesc(1, 0, args.n_mma);
       else if (PREC == PREC_I8) idesc = ptx::make_idesc(2, 1, args.n_mma);
       else idesc = ptx::make_idesc(1, 2, args.n_mma);
+      const uint64_t desc0 = ptx::sw128_kmajor_desc(0);  // every field but the address
       const uint32_t a_base = ptx::smem_addr(a_smem);
       const uint32_t b_base = ptx::smem_addr(b_smem);
       const uint32_t acc_cols = static_cast<uint32_t>(args.nrows);
-      int it = 0, tl = 0;
+      const uint32_t sub_bytes = static_cast<uint32_t>(args.n_mma) * kRowBytes;
+      const uint32_t lo_bytes = static_cast<uint32_t>(args.nrows) * kRowBytes;
+      const int nsub = args.nsub, numKB = args.numKB;
+      int s = 0, acc = 0;
+      uint32_t ph = 0, use = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x, ++tl) {
-        const int acc = tl % args.acc_bufs;
-        const uint32_t use = (tl / args.acc_bufs) & 1;
-        if (!wait_bar(tempty + 8 * acc, use ^ 1, args, abort_flag, DCNV2_DEVERR_TIMEOUT_MMA)) {
+      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
+        if (!wait_bar<64>(tempty + 8 * acc, use ^ 1, args, abort_flag, DCNV2_DEVERR_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
         ptx::tc_fence_after();
         const uint32_t d_base = tmem_base + acc * acc_cols;
-        for (int kb = 0; kb < args.numKB; ++kb, ++it) {
-          const int s = it % S;
-          const uint32_t ph = (it / S) & 1;
+        for (int kb = 0; kb < numKB; ++kb) {
           if (!wait_bar(full_a + 8 * s, ph, args, abort_flag, DCNV2_DEVERR_TIMEOUT_MMA) ||
               !wait_bar(full_b + 8 * s, ph, args, abort_flag, DCNV2_DEVERR_TIMEOUT_MMA)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          const uint32_t a_s = a_base + s * args.a_stage_bytes;
-          const uint32_t b_s = b_base + s * args.b_stage_bytes;
+          const uint64_t ad0 = desc0 | (((a_base + s * args.a_stage_bytes) >> 4) & 0x3FFFu);
+          const uint64_t bd0 = desc0 | (((b_base + s * args.b_stage_bytes) >> 4) & 0x3FFFu);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint64_t ad = ptx::sw128_kmajor_desc(a_s + 32 * k);
-            for (int sub = 0; sub < args.nsub; ++sub) {
+            const uint64_t ad = ad0 + 2 * k;  // +32 bytes per K-step (address field in 16 B)
+            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            for (int sub = 0; sub < nsub; ++sub) {
               const uint32_t d = d_base + sub * args.n_mma;
-              const uint32_t b_off = b_s + sub * args.n_mma * kRowBytes + 32 * k;
-              const uint64_t bd = ptx::sw128_kmajor_desc(b_off);
-              const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+              const uint64_t bd = bd0 + 2 * k + ((sub * sub_bytes) >> 4);
               if (PREC == PREC_F16) {
                 ptx::mma_f16(d, ad, bd, idesc, accum);
               } else if (PREC == PREC_I8) {
@@ -348,19 +408,18 @@ __global__ void __launch_bounds__(kThreads, 1) dcnv2_fused_kernel(const FusedArg
               } else {
                 ptx::mma_tf32(d, ad, bd, idesc, accum);
                 if (!args.tf32_single) {
-                  const uint64_t bd_lo =
-                      ptx::sw128_kmajor_desc(b_off + args.nrows * kRowBytes);
-                  const uint64_t ad_lo = ptx::sw128_kmajor_desc(a_s + kATileBytes + 32 * k);
-                  ptx::mma_tf32(d, ad, bd_lo, idesc, 1u);
-                  ptx::mma_tf32(d, ad_lo, bd, idesc, 1u);
+                  ptx::mma_tf32(d, ad, bd + (lo_bytes >> 4), idesc, 1u);
+                  ptx::mma_tf32(d, ad + (kATileBytes >> 4), bd, idesc, 1u);
                 }
               }
             }
           }
           ptx::tc_commit(empty + 8 * s);  // frees this stage once its MMAs have read it
+          if (++s == S) { s = 0; ph ^= 1u; }
         }
         if (!ok) break;
         ptx::tc_commit(tfull + 8 * acc);  // accumulator ready for the epilogue
+        if (++acc == args.acc_bufs) { acc = 0; use ^= 1u; }
       }
       ptx::tc_commit(drain);
       wait_bar(drain, 0, args, abort_flag, DCNV2_DEVERR_TIMEOUT_DRAIN);
@@ -374,7 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1) dcnv2_fused_kernel(const FusedArg
       const int acc = tl % args.acc_bufs;
       const uint32_t ph = (tl / args.acc_bufs) & 1;
       // Warp-uniform outcome: every lane must take part in the tcgen05.ld below or none.
-      const bool got = wait_bar(tfull + 8 * acc, ph, args, abort_flag, DCNV2_DEVERR_TIMEOUT_EPILOGUE);
+      const bool got =
+          wait_bar<256>(tfull + 8 * acc, ph, args, abort_flag, DCNV2_DEVERR_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, got)) break;
       ptx::tc_fence_after();
       int img, pt, cc;
@@ -421,114 +481,292 @@ __global__ void __launch_bounds__(kThreads, 1) dcnv2_fused_kernel(const FusedArg
     }
   } else {
     // ------------------------------------------------------------ samplers
+    // K order is (group g, channel block cbg, tap t). Thread (pixel slot ps, chunk j) fills rows
+    // ps and ps + 64, 16-byte chunk j, of every A tile.
+    // Geometry: the 8 lanes of a pixel slot own the 8 (row, corner) items of its two rows. Per
+    // (tile, group) each lane computes its item for every tap once (registers; the taps are
+    // unrolled when KT > 0) and per K-block the items of the current tap are shuffled to the 8
+    // lanes. An item is the corner weight and its location: a pixel index inside the shared-memory
+    // window of x (use_win: the 128-byte channel block of win_rows whole rows), or, when the
+    // corner lies outside the window, its pixel index in the channels-last copy of x in global
+    // memory. A corner outside the image has weight 0 and points at window / global pixel 0.
+    // For the fp16 fast path an item packs weight (low 16 bits) and window pixel (high 16 bits,
+    // 0xFFFF = not in the window) into one word. A K-block whose warp has only in-window items
+    // and full channel chunks takes a straight-line path of shared-memory loads.
+    // Each K-block issues its 8 corner loads before waiting for the A stage to be free.
     constexpr int EPC = TR::kChunkElems, KC = TR::kBlockElems, EB = TR::kElemBytes;
+    constexpr int R = kRowsPerSampThread;
+    constexpr bool kPacked = (PREC == PREC_F16 && !PRECISE);
+    constexpr uint32_t kNoWin = 0xFFFFu;
+    constexpr int kCache = KT > 0 ? KT : 1;
+    static_assert(R * 4 == 8, "one (row, corner) item per lane of a pixel-slot group");
     const int st = threadIdx.x - kSampWarp0 * 32;
+    const int sw = st >> 5;     // sampler warp
     const int j = st & 7;       // 16-byte chunk of the 128-byte row
-    const int ps = st >> 3;     // pixel slot: rows ps + 32 r
-    const uint32_t a_base = ptx::smem_addr(a_smem);
+    const int ps = st >> 3;     // pixel slot
+    const int myr = j >> 2, myc = j & 3;
+    const int grp = lane & ~7;
+    const bool issuer = args.use_win && sw == 0 && lane == 0;  // issues the window loads
     const GT* offp = reinterpret_cast<const GT*>(args.offset);
     const GT* maskp = reinterpret_cast<const GT*>(args.mask);
-    int it = 0;
+    const uint32_t w_base = ptx::smem_addr(w_smem);
+    const uint32_t a_base = ptx::smem_addr(a_smem);
+    const int cb_per_tile = args.dg * args.CBg;
+    const int T = KT > 0 ? KT : args.T;
+    // this thread's two chunk positions inside an A stage (fixed for the whole kernel)
+    uint32_t dst_off[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int m_row = ps + kSampRowStride * r;
+      dst_off[r] = m_row * kRowBytes + ((j ^ (m_row & 7)) << 4);
+    }
+    int s = 0;                  // A stage
+    uint32_t ph = 0;            // its phase
+    int cbi = 0;                // channel-block sequence number (window buffer = cbi & 1)
+    int issued = 0;             // windows issued so far (issuer)
     bool ok = true;
+
+    // Window load of channel block q of this CTA's sequence (issuer only): waits until buffer
+    // q & 1 is released by all sampler warps (its use q - 2), then one 4-D TMA box.
+    auto issue_window = [&](int q) -> bool {
+      const int k = q / cb_per_tile, r = q - k * cb_per_tile;
+      const int tl = blockIdx.x + k * gridDim.x;
+      if (tl >= args.num_tiles) return true;
+      const int g = r / args.CBg, cbg = r - g * args.CBg;
+      int im, pt, cc;
+      decode_tile(args, tl, im, pt, cc);
+      const int row0 = ((pt * kTileM) / args.Wo) * args.stride - args.win_top;
+      const int b = q & 1;
+      const uint32_t use = static_cast<uint32_t>(q >> 1) & 1u;
+      if (!wait_bar<kSuspend>(win_empty + 8 * b, use ^ 1u, args, abort_flag, DCNV2_DEVERR_TIMEOUT_SAMPLER))
+        return false;
+      ptx::mbar_arrive_expect_tx(win_full + 8 * b, args.win_bytes);
+      ptx::tma_load_4d(w_base + b * args.win_bytes, &tmap_x, (g * args.Cg + cbg * KC) * EB, 0,
+                       row0, im, win_full + 8 * b);
+      issued = q + 1;
+      return true;
+    };
+    if (issuer) ok = issue_window(0) && issue_window(1);
+    ok = __all_sync(0xffffffffu, ok);
+
     for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
       int img, pt, cc;
       decode_tile(args, tile, img, pt, cc);
-      int pix[kRowsPerSampThread], oh[kRowsPerSampThread], ow[kRowsPerSampThread];
-      bool pval[kRowsPerSampThread];
-#pragma unroll
-      for (int r = 0; r < kRowsPerSampThread; ++r) {
-        pix[r] = pt * kTileM + ps + 32 * r;
-        pval[r] = pix[r] < args.P;
-        const int pc = pval[r] ? pix[r] : 0;
-        oh[r] = pc / args.Wo;
-        ow[r] = pc - oh[r] * args.Wo;
-      }
-      const uint8_t* ximg =
-          args.x_nhwc + static_cast<size_t>(img) * args.H * args.W * args.C * EB;
-      for (int g = 0; g < args.dg && ok; ++g) {
-        for (int t = 0; t < args.T && ok; ++t) {
-          const int ki = t / args.K, kj = t - ki * args.K;
-          const size_t goff =
-              (static_cast<size_t>(img) * args.dg + g) * 2 * args.T + 2 * t;
+      const int my_pix = pt * kTileM + ps + kSampRowStride * myr;
+      const bool my_val = my_pix < args.P;
+      const int pcl = my_val ? my_pix : 0;
+      const int oh = pcl / args.Wo, ow = pcl - (pcl / args.Wo) * args.Wo;
+      const int my_bh = oh * args.stride - args.pad;
+      const int my_bw = ow * args.stride - args.pad;
+      const int row0 = ((pt * kTileM) / args.Wo) * args.stride - args.win_top;
+      const uint8_t* ximg = args.x_nhwc + static_cast<size_t>(img) * args.H * args.W * args.C * EB;
+
+      // this lane's item of tap t: weight word (packed for the fp16 fast path) and global pixel
+      auto item = [&](int g, int t, uint32_t& wword, int& gpix) {
+        const int ki = t / args.K, kj = t - ki * args.K;
+        float dh = 0.f, dw = 0.f, m = 0.f;
+        if (my_val) {
+          const size_t goff = (static_cast<size_t>(img) * args.dg + g) * 2 * args.T + 2 * t;
           const size_t gmsk = (static_cast<size_t>(img) * args.dg + g) * args.T + t;
-          float wts[kRowsPerSampThread][4];
-          int cof[kRowsPerSampThread][4];
+          dh = load_geom_value(offp + goff * args.P + my_pix);
+          dw = load_geom_value(offp + (goff + 1) * args.P + my_pix);
+          m = load_geom_value(maskp + gmsk * args.P + my_pix);
+        }
+        const float hf = __fadd_rn(static_cast<float>(my_bh + ki * args.dil), dh);
+        const float wf = __fadd_rn(static_cast<float>(my_bw + kj * args.dil), dw);
+        const bool inside = my_val && !(hf <= -1.f || hf >= static_cast<float>(args.H) ||
+                                        wf <= -1.f || wf >= static_cast<float>(args.W));
+        const float h0f = floorf(hf), w0f = floorf(wf);
+        const int h0 = inside ? static_cast<int>(h0f) : 0;
+        const int w0 = inside ? static_cast<int>(w0f) : 0;
+        const float lh = __fsub_rn(hf, h0f), lw = __fsub_rn(wf, w0f);
+        const float hh = __fsub_rn(1.f, lh), hw = __fsub_rn(1.f, lw);
+        const int dy = myc >> 1, dx = myc & 1;
+        const float fy = dy ? lh : hh, fx = dx ? lw : hw;
+        const int hc = h0 + dy, wc = w0 + dx;
+        const bool cok = inside && hc >= 0 && hc <= args.H - 1 && wc >= 0 && wc <= args.W - 1;
+        const float wt = cok ? __fmul_rn(m, __fmul_rn(fy, fx)) : 0.f;
+        gpix = cok ? hc * args.W + wc : 0;
+        uint32_t wpix = kNoWin;  // pixel inside the window
+        if (!cok) wpix = 0;
+        else if (args.use_win && hc >= row0 && hc < row0 + args.win_rows)
+          wpix = static_cast<uint32_t>((hc - row0) * args.W + wc);
+        if (!args.use_win) wpix = kNoWin;
+        if (kPacked) {
+          // high half: byte offset of the pixel in the window (windows are at most 64 KB)
+          const uint32_t hb = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(wt)));
+          wword = hb | ((wpix != kNoWin ? wpix * kRowBytes : kNoWin) << 16);
+        } else {
+          wword = __float_as_uint(wt);
+          gpix = (wpix != kNoWin) ? -static_cast<int>(wpix) - 1 : gpix;  // < 0: window pixel
+        }
+      };
+
+      for (int g = 0; g < args.dg && ok; ++g) {
+        // items of every tap, computed once per (tile, group) for 3x3 kernels
+        uint32_t cw[kCache];
+        int cg[kCache];
+        bool fast_g = false;
+        if (KT > 0) {
+          bool inwin = true;
 #pragma unroll
-          for (int r = 0; r < kRowsPerSampThread; ++r) {
-            float dh = 0.f, dw = 0.f, m = 0.f;
-            if (pval[r]) {
-              dh = load_geom_value(offp + goff * args.P + pix[r]);
-              dw = load_geom_value(offp + (goff + 1) * args.P + pix[r]);
-              m = load_geom_value(maskp + gmsk * args.P + pix[r]);
-            }
-            const Geom gm = make_geom(args, pval[r], oh[r] * args.stride - args.pad + ki * args.dil,
-                                      ow[r] * args.stride - args.pad + kj * args.dil, dh, dw, m);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              wts[r][c] = gm.a[c];
-              cof[r][c] = gm.off[c];
-            }
+          for (int t = 0; t < kCache; ++t) {
+            item(g, t, cw[t], cg[t]);
+            inwin = inwin && ((cw[t] >> 16) != kNoWin);
           }
-          uint32_t wh[kRowsPerSampThread][4];  // fp16 fast path: weights as duplicated half2
-          if (PREC == PREC_F16) {
-#pragma unroll
-            for (int r = 0; r < kRowsPerSampThread; ++r)
-#pragma unroll
-              for (int c = 0; c < 4; ++c) wh[r][c] = h2_bits(__float2half2_rn(wts[r][c]));
+          fast_g = kPacked && __all_sync(0xffffffffu, inwin);
+        }
+        const int gbase = g * args.Cg;
+        for (int cbg = 0; cbg < args.CBg && ok; ++cbg) {
+          const int b = cbi & 1;
+          if (args.use_win) {
+            const bool got = wait_bar<kSuspend>(win_full + 8 * b, static_cast<uint32_t>(cbi >> 1) & 1u,
+                                      args, abort_flag, DCNV2_DEVERR_TIMEOUT_SAMPLER);
+            if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
           }
-          for (int cbg = 0; cbg < args.CBg; ++cbg, ++it) {
-            const int s = it % S;
-            const uint32_t ph = (it / S) & 1;
-            const bool got =
-                wait_bar(empty + 8 * s, ph ^ 1, args, abort_flag, DCNV2_DEVERR_TIMEOUT_SAMPLER);
-            if (!__all_sync(0xffffffffu, got)) {
-              ok = false;
-              break;
-            }
-            const int cig = cbg * KC + j * EPC;  // channel within the group
-            const bool cvalid = cig < args.Cg;
-            const int cbase = g * args.Cg + cig;
-            const uint32_t a_s = a_base + s * args.a_stage_bytes;
+          const uint32_t win = w_base + b * args.win_bytes + j * 16;
+          const int cig = cbg * KC + j * EPC;  // channel within the group
+          const bool cvalid = cig < args.Cg;
+          const bool all_valid = (cbg + 1) * KC <= args.Cg;  // block-uniform
+          const uint8_t* gsrc = ximg + static_cast<size_t>(gbase + cig) * EB;
+          if (kPacked && fast_g && all_valid) {
+            // Fast path: every corner of every tap of this warp is in the window and every
+            // chunk is full. Straight-line per tap: 8 shuffles, 8 shared loads, mix, 2 stores.
 #pragma unroll
-            for (int r = 0; r < kRowsPerSampThread; ++r) {
-              const int m_row = ps + 32 * r;
-              const uint32_t dst = a_s + m_row * kRowBytes + ((j ^ (m_row & 7)) << 4);
-              uint4 out = make_uint4(0, 0, 0, 0), out_lo = make_uint4(0, 0, 0, 0);
-              if (cvalid) {
-                const uint4 x0 = ptx::ld_nc_v4(ximg + static_cast<size_t>(cof[r][0] + cbase) * EB);
-                const uint4 x1 = ptx::ld_nc_v4(ximg + static_cast<size_t>(cof[r][1] + cbase) * EB);
-                const uint4 x2 = ptx::ld_nc_v4(ximg + static_cast<size_t>(cof[r][2] + cbase) * EB);
-                const uint4 x3 = ptx::ld_nc_v4(ximg + static_cast<size_t>(cof[r][3] + cbase) * EB);
-                if (PREC == PREC_F16) {
-                  if (args.precise) {
-                    out.x = f16_mix_precise(wts[r], x0.x, x1.x, x2.x, x3.x);
-                    out.y = f16_mix_precise(wts[r], x0.y, x1.y, x2.y, x3.y);
-                    out.z = f16_mix_precise(wts[r], x0.z, x1.z, x2.z, x3.z);
-                    out.w = f16_mix_precise(wts[r], x0.w, x1.w, x2.w, x3.w);
-                  } else {
-                    out.x = f16_mix_fast(wh[r][0], wh[r][1], wh[r][2], wh[r][3], x0.x, x1.x, x2.x, x3.x);
-                    out.y = f16_mix_fast(wh[r][0], wh[r][1], wh[r][2], wh[r][3], x0.y, x1.y, x2.y, x3.y);
-                    out.z = f16_mix_fast(wh[r][0], wh[r][1], wh[r][2], wh[r][3], x0.z, x1.z, x2.z, x3.z);
-                    out.w = f16_mix_fast(wh[r][0], wh[r][1], wh[r][2], wh[r][3], x0.w, x1.w, x2.w, x3.w);
-                  }
-                } else if (PREC == PREC_I8) {
-                  out.x = i8_mix_word(wts[r], x0.x, x1.x, x2.x, x3.x);
-                  out.y = i8_mix_word(wts[r], x0.y, x1.y, x2.y, x3.y);
-                  out.z = i8_mix_word(wts[r], x0.z, x1.z, x2.z, x3.z);
-                  out.w = i8_mix_word(wts[r], x0.w, x1.w, x2.w, x3.w);
-                } else {
-                  f32_mix(wts[r], x0, x1, x2, x3, out, out_lo);
+            for (int tt = 0; tt < kCache; ++tt) {
+              uint32_t wv[R][4];
+              uint4 xv[R][4];
+#pragma unroll
+              for (int r = 0; r < R; ++r)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  const uint32_t v = __shfl_sync(0xffffffffu, cw[tt], grp | (r * 4 + c));
+                  wv[r][c] = v;                                   // fp16 weight in bits 0-15
+                  xv[r][c] = ptx::ld_shared_v4(win + (v >> 16));  // window byte offset
                 }
+              const bool got =
+                  wait_bar<kSuspend>(empty + 8 * s, ph ^ 1, args, abort_flag, DCNV2_DEVERR_TIMEOUT_SAMPLER);
+              if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+              const uint32_t a_s = a_base + s * args.a_stage_bytes;
+#pragma unroll
+              for (int r = 0; r < R; ++r) {
+                const __half2 w0 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[r][0])));
+                const __half2 w1 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[r][1])));
+                const __half2 w2 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[r][2])));
+                const __half2 w3 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[r][3])));
+                uint4 out;
+                out.x = f16_mix_h2(w0, w1, w2, w3, xv[r][0].x, xv[r][1].x, xv[r][2].x, xv[r][3].x);
+                out.y = f16_mix_h2(w0, w1, w2, w3, xv[r][0].y, xv[r][1].y, xv[r][2].y, xv[r][3].y);
+                out.z = f16_mix_h2(w0, w1, w2, w3, xv[r][0].z, xv[r][1].z, xv[r][2].z, xv[r][3].z);
+                out.w = f16_mix_h2(w0, w1, w2, w3, xv[r][0].w, xv[r][1].w, xv[r][2].w, xv[r][3].w);
+                ptx::st_shared_v4(a_s + dst_off[r], out);
               }
-              ptx::st_shared_v4(dst, out);
-              if (PREC == PREC_F32) ptx::st_shared_v4(dst + kATileBytes, out_lo);
+              ptx::fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) ptx::mbar_arrive(full_a + 8 * s);
+              if (++s == S) { s = 0; ph ^= 1u; }
             }
-            ptx::fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(full_a + 8 * s);
+          } else {
+            // General path (any tap count, corners outside the window, partial chunks, int8,
+            // fp32 and precise fp16): items recomputed per K-block.
+            for (int t = 0; t < T && ok; ++t) {
+              uint32_t myw;
+              int myg;
+              item(g, t, myw, myg);
+              uint32_t wv[R][4];
+              int loc[R][4];  // >= 0: window byte offset; < 0: global pixel -loc - 1
+#pragma unroll
+              for (int r = 0; r < R; ++r)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  const int src = grp | (r * 4 + c);
+                  const uint32_t v = __shfl_sync(0xffffffffu, myw, src);
+                  const int gp = __shfl_sync(0xffffffffu, myg, src);
+                  if (kPacked) {
+                    wv[r][c] = v;
+                    loc[r][c] = (v >> 16) != kNoWin ? static_cast<int>(v >> 16) : -gp - 1;
+                  } else {
+                    wv[r][c] = v;
+                    loc[r][c] = gp < 0 ? (-gp - 1) * kRowBytes : -gp - 1;
+                  }
+                }
+              const bool got =
+                  wait_bar<kSuspend>(empty + 8 * s, ph ^ 1, args, abort_flag, DCNV2_DEVERR_TIMEOUT_SAMPLER);
+              if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+              const uint32_t a_s = a_base + s * args.a_stage_bytes;
+#pragma unroll
+              for (int r = 0; r < R; ++r) {
+                uint4 xv[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  const int e = loc[r][c];
+                  if (!cvalid) {
+                    xv[c] = make_uint4(0, 0, 0, 0);
+                  } else if (e >= 0) {
+                    xv[c] = ptx::ld_shared_v4(win + e);
+                  } else {
+                    xv[c] = ptx::ld_nc_v4(gsrc + static_cast<size_t>(-e - 1) * args.C * EB);
+                  }
+                }
+                uint4 out = make_uint4(0, 0, 0, 0), out_lo = make_uint4(0, 0, 0, 0);
+                if (cvalid) {
+                  const uint4& x0 = xv[0];
+                  const uint4& x1 = xv[1];
+                  const uint4& x2 = xv[2];
+                  const uint4& x3 = xv[3];
+                  if (kPacked) {
+                    const __half2 w0 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[r][0])));
+                    const __half2 w1 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[r][1])));
+                    const __half2 w2 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[r][2])));
+                    const __half2 w3 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[r][3])));
+                    out.x = f16_mix_h2(w0, w1, w2, w3, x0.x, x1.x, x2.x, x3.x);
+                    out.y = f16_mix_h2(w0, w1, w2, w3, x0.y, x1.y, x2.y, x3.y);
+                    out.z = f16_mix_h2(w0, w1, w2, w3, x0.z, x1.z, x2.z, x3.z);
+                    out.w = f16_mix_h2(w0, w1, w2, w3, x0.w, x1.w, x2.w, x3.w);
+                  } else {
+                    const float wf4[4] = {__uint_as_float(wv[r][0]), __uint_as_float(wv[r][1]),
+                                          __uint_as_float(wv[r][2]), __uint_as_float(wv[r][3])};
+                    if (PREC == PREC_F16) {
+                      out.x = f16_mix_precise(wf4, x0.x, x1.x, x2.x, x3.x);
+                      out.y = f16_mix_precise(wf4, x0.y, x1.y, x2.y, x3.y);
+                      out.z = f16_mix_precise(wf4, x0.z, x1.z, x2.z, x3.z);
+                      out.w = f16_mix_precise(wf4, x0.w, x1.w, x2.w, x3.w);
+                    } else if (PREC == PREC_I8) {
+                      out.x = i8_mix_word(wf4, x0.x, x1.x, x2.x, x3.x);
+                      out.y = i8_mix_word(wf4, x0.y, x1.y, x2.y, x3.y);
+                      out.z = i8_mix_word(wf4, x0.z, x1.z, x2.z, x3.z);
+                      out.w = i8_mix_word(wf4, x0.w, x1.w, x2.w, x3.w);
+                    } else {
+                      f32_mix(wf4, x0, x1, x2, x3, out, out_lo);
+                    }
+                  }
+                }
+                ptx::st_shared_v4(a_s + dst_off[r], out);
+                if (PREC == PREC_F32) ptx::st_shared_v4(a_s + dst_off[r] + kATileBytes, out_lo);
+              }
+              ptx::fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) ptx::mbar_arrive(full_a + 8 * s);
+              if (++s == S) { s = 0; ph ^= 1u; }
+            }
           }
+          if (!ok) break;
+          if (args.use_win) {
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(win_empty + 8 * b);
+            bool iok = true;
+            if (issuer) iok = issue_window(cbi + 2);
+            if (!__all_sync(0xffffffffu, iok)) { ok = false; break; }
+          }
+          ++cbi;
         }
       }
+    }
+    // Window loads still in flight (only after an abort) must land before the CTA exits.
+    if (issuer) {
+      for (int q = issued - 2 < 0 ? 0 : issued - 2; q < issued; ++q)
+        wait_bar(win_full + 8 * (q & 1), static_cast<uint32_t>(q >> 1) & 1u, args, abort_flag,
+                 DCNV2_DEVERR_TIMEOUT_DRAIN);
     }
   }
 
@@ -542,59 +780,56 @@ __global__ void __launch_bounds__(kThreads, 1) dcnv2_fused_kernel(const FusedArg
 }
 
 // ------------------------------------------------------------------ pre-pass: NCHW -> NHWC
-// One 32-bit word moves VEC = 4/sizeof(T) elements; tile = (32*VEC) channels x (32*VEC) pixels.
+// One 16-byte vector moves V = 16/sizeof(T) elements; a tile is TILE = 8*V channels by TILE
+// pixels (128-byte rows both ways: 64x64 fp16, 128x128 int8, 32x32 fp32). Rows of the shared
+// tile are padded by 4 bytes so that the column reads of the store phase spread over banks.
 template <typename T>
 __global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const T* __restrict__ x,
                                                            T* __restrict__ xt, int C, int HW) {
-  constexpr int VEC = 4 / sizeof(T);
-  constexpr int TILE = 32 * VEC;
-  __shared__ T tile[TILE][TILE + VEC];
+  constexpr int V = 16 / sizeof(T);
+  constexpr int TILE = 8 * V;
+  constexpr int PAD = 4 / sizeof(T);
+  __shared__ T tile[TILE][TILE + PAD];
   const int n = blockIdx.z;
   const int c0 = blockIdx.y * TILE, p0 = blockIdx.x * TILE;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const T* xs = x + static_cast<size_t>(n) * C * HW;
   T* xd = xt + static_cast<size_t>(n) * C * HW;
-  const bool vec_ok = (HW % VEC) == 0 && (p0 + TILE) <= HW &&
-                      (reinterpret_cast<uintptr_t>(x) & 3u) == 0;
-  for (int i = ty; i < TILE; i += 8) {
+  const bool vec_in = (HW % V) == 0 && (p0 + TILE) <= HW &&
+                      (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+  for (int idx = threadIdx.x; idx < TILE * 8; idx += 256) {
+    const int i = idx >> 3, q = idx & 7;  // channel row i, 16-byte chunk q of pixels
     const int c = c0 + i;
-    if (c < C) {
-      const T* row = xs + static_cast<size_t>(c) * HW + p0;
-      if (vec_ok) {
-        const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(row) + tx);
-        const T* e = reinterpret_cast<const T*>(&w);
+    if (c < C && vec_in) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(xs + static_cast<size_t>(c) * HW + p0) + q);
+      const T* e = reinterpret_cast<const T*>(&v);
 #pragma unroll
-        for (int k = 0; k < VEC; ++k) tile[i][tx * VEC + k] = e[k];
-      } else {
-#pragma unroll
-        for (int k = 0; k < VEC; ++k) {
-          const int p = tx * VEC + k;
-          tile[i][p] = (p0 + p < HW) ? row[p] : T(0);
-        }
-      }
+      for (int k = 0; k < V; ++k) tile[i][q * V + k] = e[k];
     } else {
 #pragma unroll
-      for (int k = 0; k < VEC; ++k) tile[i][tx * VEC + k] = T(0);
+      for (int k = 0; k < V; ++k) {
+        const int p = p0 + q * V + k;
+        tile[i][q * V + k] = (c < C && p < HW) ? xs[static_cast<size_t>(c) * HW + p] : T(0);
+      }
     }
   }
   __syncthreads();
-  const bool cvec_ok = (C % VEC) == 0 && (c0 + TILE) <= C &&
-                       (reinterpret_cast<uintptr_t>(xt) & 3u) == 0;
-  for (int i = ty; i < TILE; i += 8) {
+  const bool vec_out = (C % V) == 0 && (c0 + TILE) <= C &&
+                       (reinterpret_cast<uintptr_t>(xt) & 15u) == 0;
+  for (int idx = threadIdx.x; idx < TILE * 8; idx += 256) {
+    const int i = idx >> 3, q = idx & 7;  // pixel row i, 16-byte chunk q of channels
     const int p = p0 + i;
     if (p >= HW) continue;
-    T* row = xd + static_cast<size_t>(p) * C + c0;
-    if (cvec_ok) {
-      uint32_t w;
-      T* e = reinterpret_cast<T*>(&w);
+    if (vec_out) {
+      uint4 v;
+      T* e = reinterpret_cast<T*>(&v);
 #pragma unroll
-      for (int k = 0; k < VEC; ++k) e[k] = tile[tx * VEC + k][i];
-      reinterpret_cast<uint32_t*>(row)[tx] = w;
+      for (int k = 0; k < V; ++k) e[k] = tile[q * V + k][i];
+      reinterpret_cast<uint4*>(xd + static_cast<size_t>(p) * C + c0)[q] = v;
     } else {
 #pragma unroll
-      for (int k = 0; k < VEC; ++k) {
-        const int c = tx * VEC + k;
-        if (c0 + c < C) row[c] = tile[c][i];
+      for (int k = 0; k < V; ++k) {
+        const int c = c0 + q * V + k;
+        if (c < C) xd[static_cast<size_t>(p) * C + c] = tile[q * V + k][i];
       }
     }
   }
@@ -603,7 +838,7 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const T* __restrict__
 // ------------------------------------------------------------------ pre-pass: weight pack
 // Writes, for every (cout chunk, K-block), the B operand tile exactly as it must sit in shared
 // memory: row o (output channel), 16-byte chunk jc at chunk jc ^ (o % 8) of the 128-byte row.
-// K-block kb = (g*T + t)*CBg + cbg holds channels g*Cg + cbg*KC + [0, KC) of tap t.
+// K-block kb = (g*CBg + cbg)*T + t holds channels g*Cg + cbg*KC + [0, KC) of tap t.
 // Also clears the device error word for the fused kernel that follows.
 template <int PREC>
 __global__ void __launch_bounds__(256) pack_weights_kernel(const void* __restrict__ w,
@@ -622,8 +857,8 @@ __global__ void __launch_bounds__(256) pack_weights_kernel(const void* __restric
     const size_t blk = (idx >> 3) / nrows;  // cc * numKB + kb
     const int kb = static_cast<int>(blk % numKB);
     const int cc = static_cast<int>(blk / numKB);
-    const int cbg = kb % CBg;
-    const int t = (kb / CBg) % T;
+    const int t = kb % T;
+    const int cbg = (kb / T) % CBg;
     const int g = kb / (CBg * T);
     const int o = cc * nrows + row;
     const size_t tile_base = blk * TR::kNumBTiles * nrows * kRowBytes;

@@ -37,6 +37,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Same test, but the thread may be suspended for up to `suspend_ns` while the phase is
+// incomplete (it resumes as soon as the phase completes), so waiting warps do not spin.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity,
+                                                    uint32_t suspend_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -53,6 +67,19 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
       "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// 4-D tiled TMA load of one box of `tmap` at coordinates {c0, c1, c2, c3} (innermost first) into
+// CTA-local shared memory, completing its bytes on `bar`. c0 * element size must be a multiple of
+// 16 bytes; other coordinates may be negative or out of range (the box reads zeros there).
+// No multicast.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int c0, int c1, int c2,
+                                            int c3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
       : "memory");
 }
 
@@ -160,10 +187,25 @@ __device__ __forceinline__ uint32_t cvt_rna_tf32(float v) {
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
 }
+// Shared-memory load by 32-bit shared address. volatile keeps it after the (volatile) barrier
+// wait that precedes it in program order.
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_shared_u32_volatile(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.volatile.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+// Shared-memory store by 32-bit shared address (volatile: stays before the proxy fence and the
+// mbarrier arrive that publish it).
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
-               "r"(v.z), "r"(v.w)
-               : "memory");
+               "r"(v.z), "r"(v.w));
 }
 
 }  // namespace ptx
