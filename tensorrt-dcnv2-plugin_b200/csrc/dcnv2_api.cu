@@ -34,6 +34,7 @@ struct DevInfo {
   int minor = 0;
   bool ok = false;
   std::atomic<uint32_t> attr_set{0};
+  std::atomic<int> pair_clusters[3] = {{0}, {0}, {0}};  // co-resident CTA pairs, per precision
 };
 constexpr int kMaxDevices = 64;
 DevInfo g_dev[kMaxDevices];
@@ -95,7 +96,9 @@ struct Plan {
   // fused-kernel configuration
   int CBg = 0, numKB = 0, cchunks = 0, nrows = 0, nsub = 0, n_mma = 0, acc_bufs = 0;
   int stages = 0, tiles_per_img = 0, num_tiles = 0;
-  uint32_t tmem_cols = 0, a_stage_bytes = 0, b_stage_bytes = 0;
+  bool pair = false;  // CTA pairs (cta_group::2), tiles of 256 pixels
+  uint32_t tmem_cols = 0, a_stage_bytes = 0, b_stage_bytes = 0;  // per CTA
+  size_t b_kb_bytes = 0;  // packed weights of one K-block (both halves of a pair)
   size_t smem_bytes = 0;
   // fp32-exact kernel configuration
   int x_ptiles = 0, x_ctiles = 0;
@@ -190,13 +193,20 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
     uint32_t cols = 32;
     while (cols < static_cast<uint32_t>(p.acc_bufs * p.nrows)) cols <<= 1;
     p.tmem_cols = cols;
+    // fp16 / int8 can run as CTA pairs (M = 256 per MMA, each CTA holding half of B): opt-in
+    // with the environment variable DCNV2_PAIR=1. One CTA per tile is the default, measured
+    // faster on the 256-channel layers (the pair adds a cross-CTA hand-off to every K-block).
+    const char* pe = std::getenv("DCNV2_PAIR");
+    p.pair = (prec == PREC_F16 || prec == PREC_I8) && pe && pe[0] == '1' && pe[1] == 0;
     p.a_stage_bytes = static_cast<uint32_t>(nA * kATileBytes);
-    p.b_stage_bytes = static_cast<uint32_t>(nB * p.nrows * kRowBytes);
+    p.b_kb_bytes = size_t(nB) * p.nrows * kRowBytes;
+    p.b_stage_bytes = static_cast<uint32_t>(p.b_kb_bytes / (p.pair ? 2 : 1));
     const size_t per_stage = p.a_stage_bytes + p.b_stage_bytes;
     const size_t fixed = 1024 + 512;  // alignment slack + barriers and flags
     int stages = static_cast<int>((kSmemLimit - fixed) / per_stage);
     if (stages > kMaxStages) stages = kMaxStages;
-    const int64_t tiles_per_img = cdiv(P, kTileM);
+    const int64_t cta_tiles_per_img = cdiv(P, kTileM);
+    const int64_t tiles_per_img = p.pair ? cdiv(P, 2 * kTileM) : cta_tiles_per_img;
     const int64_t num_tiles = int64_t(p.N) * tiles_per_img * p.cchunks;
     if (stages < 2 || numKB >= (int64_t(1) << 31) || num_tiles >= (int64_t(1) << 31)) {
       p.fused = false;
@@ -207,33 +217,38 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
       p.num_tiles = static_cast<int>(num_tiles);
       p.smem_bytes = fixed + size_t(stages) * per_stage;
       // Window of x: whole rows (W <= 256, one TMA box) covering every tap of every pixel of a
-      // tile whose offsets lie in (-1 - M, 1 + M), for the largest margin M <= 2 that still
-      // leaves two pipeline stages. Corners outside it are read from global memory.
+      // CTA's 128 pixels whose offsets lie in (-1 - M, 1 + M), for the largest margin M <= 2
+      // that still leaves three pipeline stages (else two). Corners outside it are read from
+      // global memory.
       if (p.W <= 256) {
         int rows_max = 0;
-        const int64_t loop = tiles_per_img < 4096 ? tiles_per_img : 4096;
+        const int64_t loop = cta_tiles_per_img < 4096 ? cta_tiles_per_img : 4096;
         for (int64_t pt = 0; pt < loop; ++pt) {
           const int64_t a0 = pt * kTileM, a1 = (a0 + kTileM < P ? a0 + kTileM : P) - 1;
           const int rows = static_cast<int>(a1 / p.Wo - a0 / p.Wo + 1);
           if (rows > rows_max) rows_max = rows;
         }
-        if (tiles_per_img > 4096 && p.Wo > 4096) rows_max = 1 << 20;  // no exact bound: no window
+        if (cta_tiles_per_img > 4096 && p.Wo > 4096) rows_max = 1 << 20;  // no exact bound
         const int64_t base = int64_t(rows_max - 1) * p.stride + int64_t(p.K - 1) * p.dil + 3;
-        for (int M = 2; M >= 0; --M) {
-          const int64_t rows = base + 2 * M;
-          if (rows > 256) continue;
-          const size_t wb = size_t(rows) * p.W * kRowBytes;
-          // window byte offsets travel in 16 bits; two stages at least
-          if (wb > 65536 || 2 * wb + fixed + 2 * per_stage > kSmemLimit) continue;
-          int sw = static_cast<int>((kSmemLimit - fixed - 2 * wb) / per_stage);
-          if (sw > kMaxStages) sw = kMaxStages;
-          p.use_win = true;
-          p.win_rows = static_cast<int>(rows);
-          p.win_top = p.pad + 1 + M;
-          p.win_bytes = static_cast<uint32_t>(wb);
-          p.stages = sw;
-          p.smem_bytes = fixed + size_t(sw) * per_stage + 2 * wb;
-          break;
+        bool done = false;
+        for (int want = 3; want >= 2 && !done; --want) {
+          for (int M = 2; M >= 0; --M) {
+            const int64_t rows = base + 2 * M;
+            if (rows > 256) continue;
+            const size_t wb = size_t(rows) * p.W * kRowBytes;
+            // window byte offsets travel in 16 bits
+            if (wb > 65536 || 2 * wb + fixed + size_t(want) * per_stage > kSmemLimit) continue;
+            int sw = static_cast<int>((kSmemLimit - fixed - 2 * wb) / per_stage);
+            if (sw > kMaxStages) sw = kMaxStages;
+            p.use_win = true;
+            p.win_rows = static_cast<int>(rows);
+            p.win_top = p.pad + 1 + M;
+            p.win_bytes = static_cast<uint32_t>(wb);
+            p.stages = sw;
+            p.smem_bytes = fixed + size_t(sw) * per_stage + 2 * wb;
+            done = true;
+            break;
+          }
         }
       }
     }
@@ -246,7 +261,7 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
     p.off_x = off;
     off = align_up(off + size_t(p.N) * plane * p.elem_bytes, 1024);
     p.off_w = off;
-    off += size_t(p.cchunks) * p.numKB * p.b_stage_bytes;
+    off += size_t(p.cchunks) * p.numKB * p.b_kb_bytes;
   } else if (p.kind == KIND_F32_EXACT) {
     p.off_x = off;
     off = align_up(off + size_t(p.N) * plane * sizeof(float), 1024);
@@ -257,22 +272,52 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
   return DCNV2_OK;
 }
 
+using FusedFn = void (*)(const FusedArgs, const CUtensorMap);
+
+template <typename F>
+bool set_smem_attr(F* kfn) {
+  return cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kSmemLimit)) == cudaSuccess;
+}
+
+// Launch configuration of a grid of CTA pairs (clusters of 2 along x). The attribute lives in a
+// static array, so callers copy it before changing the configuration.
+cudaLaunchConfig_t pair_launch_config(int grid, size_t smem, cudaStream_t st) {
+  static cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
 template <int PREC>
 dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, const void* offset,
                           const void* mask, const void* weight, const void* bias, void* y,
                           uint8_t* ws, float scale, cudaStream_t st, Marks& mk) {
   using TR = PrecTraits<PREC>;
   using XT = typename TR::X;
+  constexpr bool kCanPair = PREC == PREC_F16 || PREC == PREC_I8;
   const uint32_t bit = 1u << PREC;
   if (!(di->attr_set.load(std::memory_order_acquire) & bit)) {
-    const int lim = static_cast<int>(kSmemLimit);
-    const cudaFuncAttribute at = cudaFuncAttributeMaxDynamicSharedMemorySize;
-    if (cudaFuncSetAttribute(dcnv2_fused_kernel<PREC, false, 9>, at, lim) != cudaSuccess ||
-        cudaFuncSetAttribute(dcnv2_fused_kernel<PREC, false, 0>, at, lim) != cudaSuccess ||
-        (PREC == PREC_F16 &&
-         (cudaFuncSetAttribute(dcnv2_fused_kernel<PREC, true, 9>, at, lim) != cudaSuccess ||
-          cudaFuncSetAttribute(dcnv2_fused_kernel<PREC, true, 0>, at, lim) != cudaSuccess)))
-      return DCNV2_ERR_CUDA;
+    bool ok = set_smem_attr(dcnv2_fused_kernel<PREC, false, 9, false>) &&
+              set_smem_attr(dcnv2_fused_kernel<PREC, false, 0, false>);
+    if constexpr (kCanPair)
+      ok = ok && set_smem_attr(dcnv2_fused_kernel<PREC, false, 9, true>) &&
+           set_smem_attr(dcnv2_fused_kernel<PREC, false, 0, true>);
+    if constexpr (PREC == PREC_F16)
+      ok = ok && set_smem_attr(dcnv2_fused_kernel<PREC, true, 9, false>) &&
+           set_smem_attr(dcnv2_fused_kernel<PREC, true, 0, false>) &&
+           set_smem_attr(dcnv2_fused_kernel<PREC, true, 9, true>) &&
+           set_smem_attr(dcnv2_fused_kernel<PREC, true, 0, true>);
+    if (!ok) return DCNV2_ERR_CUDA;
     di->attr_set.fetch_or(bit, std::memory_order_acq_rel);
   }
   (void)dev;
@@ -311,7 +356,8 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
     if (blocks < 1) blocks = 1;
     mk.mark(st);
     pack_weights_kernel<PREC><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
-        weight, wpack, err, p.O, p.C, p.T, p.Cg, p.CBg, p.numKB, p.nrows, p.cchunks);
+        weight, wpack, err, p.O, p.C, p.T, p.Cg, p.CBg, p.numKB, p.nrows, p.cchunks,
+        p.pair ? p.n_mma / 2 : 0);
   }
   // 3) the fused implicit GEMM
   FusedArgs a;
@@ -347,17 +393,47 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
       a.use_win = 1;  // otherwise every corner is read from global memory
   }
-  const int grid = p.num_tiles < di->sm_count ? p.num_tiles : di->sm_count;
   mk.mark(st);
   // 3x3 kernels take the variant with the nine taps unrolled
   const bool k3 = p.T == 9;
-  if (PREC == PREC_F16 && p.precise) {
-    if (k3) dcnv2_fused_kernel<PREC, true, 9><<<grid, kThreads, p.smem_bytes, st>>>(a, tmap);
-    else dcnv2_fused_kernel<PREC, true, 0><<<grid, kThreads, p.smem_bytes, st>>>(a, tmap);
-  } else {
-    if (k3) dcnv2_fused_kernel<PREC, false, 9><<<grid, kThreads, p.smem_bytes, st>>>(a, tmap);
-    else dcnv2_fused_kernel<PREC, false, 0><<<grid, kThreads, p.smem_bytes, st>>>(a, tmap);
+  cudaError_t e = cudaSuccess;
+  if constexpr (kCanPair) {
+    if (p.pair) {
+      FusedFn kfn = k3 ? dcnv2_fused_kernel<PREC, false, 9, true>
+                       : dcnv2_fused_kernel<PREC, false, 0, true>;
+      if constexpr (PREC == PREC_F16) {
+        if (p.precise)
+          kfn = k3 ? dcnv2_fused_kernel<PREC, true, 9, true> : dcnv2_fused_kernel<PREC, true, 0, true>;
+      }
+      int clusters = di->pair_clusters[PREC].load(std::memory_order_acquire);
+      if (clusters <= 0) {
+        // co-resident CTA pairs of this kernel (one CTA per SM); a persistent grid of that size
+        cudaLaunchConfig_t qc = pair_launch_config(1, p.smem_bytes, st);
+        cudaLaunchAttribute qa = qc.attrs[0];
+        qc.attrs = &qa;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kfn, &qc) != cudaSuccess || clusters < 1) {
+          cudaGetLastError();
+          clusters = di->sm_count / 2;
+        }
+        di->pair_clusters[PREC].store(clusters, std::memory_order_release);
+      }
+      const int nc = p.num_tiles < clusters ? p.num_tiles : clusters;
+      cudaLaunchConfig_t cfg = pair_launch_config(2 * nc, p.smem_bytes, st);
+      cudaLaunchAttribute at = cfg.attrs[0];
+      cfg.attrs = &at;
+      e = cudaLaunchKernelEx(&cfg, kfn, a, tmap);
+      mk.mark(st);
+      return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
+    }
   }
+  const int grid = p.num_tiles < di->sm_count ? p.num_tiles : di->sm_count;
+  FusedFn kfn = k3 ? dcnv2_fused_kernel<PREC, false, 9, false>
+                   : dcnv2_fused_kernel<PREC, false, 0, false>;
+  if constexpr (PREC == PREC_F16) {
+    if (p.precise)
+      kfn = k3 ? dcnv2_fused_kernel<PREC, true, 9, false> : dcnv2_fused_kernel<PREC, true, 0, false>;
+  }
+  kfn<<<grid, kThreads, p.smem_bytes, st>>>(a, tmap);
   mk.mark(st);
   return cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
 }
@@ -435,12 +511,10 @@ __global__ void selftest_timeout_kernel(int* err, unsigned long long timeout_ns)
     ptx::fence_mbar_init();
   }
   __syncthreads();
-  FusedArgs a = {};
-  a.err = err;
-  a.timeout_ns = timeout_ns;
+  const WaitCtx wc{timeout_ns, err, &abort_flag};
   if (threadIdx.x == 0) {
     // Parity 0 of a fresh barrier completes only after one arrival, which never comes.
-    if (!wait_bar(ptx::smem_addr(&bar), 0, a, &abort_flag, DCNV2_DEVERR_TIMEOUT_MMA)) {
+    if (!wait_bar(ptx::smem_addr(&bar), 0, wc, DCNV2_DEVERR_TIMEOUT_MMA)) {
       // the error bit is already set by wait_bar
     }
     // Complete the phase so that the barrier is left in a clean state.

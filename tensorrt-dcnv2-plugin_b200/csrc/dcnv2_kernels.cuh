@@ -73,17 +73,18 @@ struct FusedArgs {
   const uint8_t* x_nhwc;   // [N][H][W][C] channels-last copy of x
   const void* offset;      // [N][dg*2*T][Ho][Wo]
   const void* mask;        // [N][dg*T][Ho][Wo]
-  const uint8_t* wpack;    // [cchunks][numKB][kNumBTiles][nrows][128 B], pre-swizzled
+  const uint8_t* wpack;    // [cchunks][numKB][kNumBTiles][nrows][128 B], pre-swizzled; for a
+                           // CTA pair each K-block is [rank][nsub][n_mma/2][128 B]
   const void* bias;        // [O] or null
   void* y;                 // [N][O][Ho][Wo]
   int* err;                // device error word
   int N, C, H, W, O, Ho, Wo, P;
   int K, T, stride, pad, dil, dg, Cg, CBg, numKB;
-  int tiles_per_img, cchunks, num_tiles;
+  int tiles_per_img, cchunks, num_tiles;  // tiles of 128 pixels (256 for a CTA pair)
   int n_mma, nsub, nrows, acc_bufs;
   int stages;
   uint32_t tmem_cols;
-  uint32_t a_stage_bytes, b_stage_bytes;
+  uint32_t a_stage_bytes, b_stage_bytes;  // per CTA (a pair's CTA holds half of the B rows)
   float scale;             // int8: x_scale * w_scale
   int use_win;             // 1: corners come from a shared-memory window of x (TMA)
   int win_rows;            // rows of x in one window (all W columns, 128 bytes per pixel)
@@ -101,24 +102,32 @@ struct FusedArgs {
 // SLEEP_NS > 0 adds a nanosleep between tries; SLEEP_NS < 0 (kSuspend) lets the hardware suspend
 // the thread until the phase completes; 0 spins (the MMA issuer, whose wake-up latency is on the
 // critical path). Waiting warps that do not spin leave the issue slots to the working ones.
+// CL selects a cluster-scope acquire (barriers that the peer CTA of a pair arrives on).
 constexpr int kSuspend = -1;
-template <int SLEEP_NS = 0>
-__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const FusedArgs& a,
-                                         volatile int* abort_flag, int code) {
-  if (ptx::mbar_try_wait(bar, parity)) return true;
+struct WaitCtx {
+  unsigned long long timeout_ns;
+  int* err;                  // device error word
+  volatile int* abort_flag;  // this CTA's abort flag (shared memory)
+};
+template <int SLEEP_NS = 0, bool CL = false>
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const WaitCtx& w,
+                                         int code) {
+  if (CL ? ptx::mbar_try_wait_cluster(bar, parity) : ptx::mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = ptx::global_timer_ns();
   for (uint32_t n = 1;; ++n) {
     if constexpr (SLEEP_NS > 0) __nanosleep(static_cast<unsigned>(SLEEP_NS));
-    if constexpr (SLEEP_NS < 0) {
+    if constexpr (CL) {
+      if (ptx::mbar_try_wait_cluster(bar, parity)) return true;
+    } else if constexpr (SLEEP_NS < 0) {
       if (ptx::mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
     } else {
       if (ptx::mbar_try_wait(bar, parity)) return true;
     }
     if ((n & 15u) == 0) {
-      if (*abort_flag) return false;
-      if (ptx::global_timer_ns() - t0 > a.timeout_ns) {
-        *abort_flag = 1;
-        atomicOr(a.err, code);
+      if (*w.abort_flag) return false;
+      if (ptx::global_timer_ns() - t0 > w.timeout_ns) {
+        *w.abort_flag = 1;
+        atomicOr(w.err, code);
         return false;
       }
     }
@@ -273,8 +282,102 @@ __device__ __forceinline__ void f32_mix(const float (&a)[4], const uint4& x0, co
   }
 }
 
+// ------------------------------------------------------------------ MMA issuer
+// One thread on the critical path, in a function of its own (not inlined) so that its loop keeps
+// its own registers whatever the sampler code around it needs. It spins on the stage barriers
+// (the samplers suspend), keeps stage and phase counters incrementally and only patches the
+// start-address field of the descriptors. The MMAs of a K-block are straight-line code: the
+// number of sub-MMAs (NSUB) and the 3xTF32 choice are template parameters, because a runtime
+// loop or branch around tcgen05.mma in this single-lane loop measured ~1.7x slower per K-block.
+struct MmaParams {
+  uint32_t a_base, b_base, a_stage_bytes, b_stage_bytes, tmem_base;
+  uint32_t full_a, full_b, full_peer, empty, tfull, tempty, drain;
+  int S, num_tiles, tile0, tstep, numKB, n_mma, nrows, acc_bufs;
+  WaitCtx wc;
+};
+
+template <int PREC, bool PAIR, int NSUB, bool TF32_SINGLE>
+__device__ __noinline__ void mma_issuer(const MmaParams mp) {
+  const uint32_t m = PAIR ? 2 * kTileM : kTileM;
+  uint32_t idesc;
+  if (PREC == PREC_F16) idesc = ptx::make_idesc(1, 0, mp.n_mma, m);
+  else if (PREC == PREC_I8) idesc = ptx::make_idesc(2, 1, mp.n_mma, m);
+  else idesc = ptx::make_idesc(1, 2, mp.n_mma, m);
+  const uint64_t desc0 = ptx::sw128_kmajor_desc(0);  // every field but the address
+  const uint32_t acc_cols = static_cast<uint32_t>(mp.nrows);
+  // B rows of one sub-MMA in this CTA's stage (a pair's CTA holds n_mma / 2 of them)
+  const uint32_t sub_bytes = static_cast<uint32_t>(PAIR ? mp.n_mma / 2 : mp.n_mma) * kRowBytes;
+  const uint32_t lo_bytes = static_cast<uint32_t>(mp.nrows) * kRowBytes;
+  const WaitCtx& wc = mp.wc;
+  const int S = mp.S, numKB = mp.numKB;
+  int s = 0, acc = 0;
+  uint32_t ph = 0, use = 0;
+  bool ok = true;
+  for (int tile = mp.tile0; tile < mp.num_tiles && ok; tile += mp.tstep) {
+    if (!wait_bar<64, PAIR>(mp.tempty + 8 * acc, use ^ 1, wc, DCNV2_DEVERR_TIMEOUT_MMA)) {
+      ok = false;
+      break;
+    }
+    ptx::tc_fence_after();
+    const uint32_t d_base = mp.tmem_base + acc * acc_cols;
+    for (int kb = 0; kb < numKB; ++kb) {
+      if (!wait_bar(mp.full_a + 8 * s, ph, wc, DCNV2_DEVERR_TIMEOUT_MMA) ||
+          !wait_bar(mp.full_b + 8 * s, ph, wc, DCNV2_DEVERR_TIMEOUT_MMA) ||
+          (PAIR && !wait_bar<0, true>(mp.full_peer + 8 * s, ph, wc, DCNV2_DEVERR_TIMEOUT_MMA))) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      const uint64_t ad0 = desc0 | (((mp.a_base + s * mp.a_stage_bytes) >> 4) & 0x3FFFu);
+      const uint64_t bd0 = desc0 | (((mp.b_base + s * mp.b_stage_bytes) >> 4) & 0x3FFFu);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint64_t ad = ad0 + 2 * k;  // +32 bytes per K-step (address field in 16 B)
+        const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+#pragma unroll
+        for (int sub = 0; sub < NSUB; ++sub) {
+          const uint32_t d = d_base + sub * mp.n_mma;
+          const uint64_t bd = bd0 + 2 * k + ((sub * sub_bytes) >> 4);
+          if (PAIR) {
+            if (PREC == PREC_F16) ptx::mma_f16_pair(d, ad, bd, idesc, accum);
+            else ptx::mma_i8_pair(d, ad, bd, idesc, accum);
+          } else if (PREC == PREC_F16) {
+            ptx::mma_f16(d, ad, bd, idesc, accum);
+          } else if (PREC == PREC_I8) {
+            ptx::mma_i8(d, ad, bd, idesc, accum);
+          } else {
+            ptx::mma_tf32(d, ad, bd, idesc, accum);
+            if (!TF32_SINGLE) {
+              ptx::mma_tf32(d, ad, bd + (lo_bytes >> 4), idesc, 1u);
+              ptx::mma_tf32(d, ad + (kATileBytes >> 4), bd, idesc, 1u);
+            }
+          }
+        }
+      }
+      // frees this stage (in both CTAs of a pair) once its MMAs have read it
+      if (PAIR) ptx::tc_commit_pair(mp.empty + 8 * s, 3);
+      else ptx::tc_commit(mp.empty + 8 * s);
+      if (++s == S) { s = 0; ph ^= 1u; }
+    }
+    if (!ok) break;
+    // accumulator ready for the epilogue(s)
+    if (PAIR) ptx::tc_commit_pair(mp.tfull + 8 * acc, 3);
+    else ptx::tc_commit(mp.tfull + 8 * acc);
+    if (++acc == mp.acc_bufs) { acc = 0; use ^= 1u; }
+  }
+  if (PAIR) ptx::tc_commit_pair(mp.drain, 3);
+  else ptx::tc_commit(mp.drain);
+  wait_bar(mp.drain, 0, wc, DCNV2_DEVERR_TIMEOUT_DRAIN);
+}
+
 // ------------------------------------------------------------------ the fused kernel
-template <int PREC, bool PRECISE, int KT>
+// PAIR: launched as clusters of two CTAs that share each tile of 256 pixels (cta_group::2).
+// Rank 0 (the leader) issues M = 256 MMAs reading rows 0-127 of A and B rows [0, N/2) from its own
+// shared memory and rows 128-255 / [N/2, N) from the same offsets in rank 1; both CTAs sample their
+// own 128 pixels, copy their half of the weights and run their own epilogue on their TMEM half.
+// Rank 1's MMA thread relays "stage full" to the leader; the leader's completion commits arrive on
+// the barriers of both CTAs.
+template <int PREC, bool PRECISE, int KT, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     dcnv2_fused_kernel(const FusedArgs args, const __grid_constant__ CUtensorMap tmap_x) {
   using TR = PrecTraits<PREC>;
@@ -292,23 +395,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t full_a = ptx::smem_addr(bars);          // [S]
   const uint32_t full_b = full_a + 8 * S;                // [S]
   const uint32_t empty = full_b + 8 * S;                 // [S]
-  const uint32_t tfull = empty + 8 * S;                  // [2]
+  const uint32_t full_peer = empty + 8 * S;              // [S] (pair leader: stage full in rank 1)
+  const uint32_t tfull = full_peer + 8 * S;              // [2]
   const uint32_t tempty = tfull + 16;                    // [2]
   const uint32_t drain = tempty + 16;                    // [1]
   const uint32_t win_full = drain + 8;                   // [2]
   const uint32_t win_empty = win_full + 16;              // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 9);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * S + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const WaitCtx wc{args.timeout_ns, args.err, abort_flag};
+  // Tile schedule: CTAs (pairs) stride over the tiles. pix_base(pt) is the first pixel of this
+  // CTA's 128 rows in tile pt.
+  const int rank = PAIR ? static_cast<int>(ptx::cluster_ctarank()) : 0;
+  const int tile0 = PAIR ? static_cast<int>(ptx::cluster_id_x()) : static_cast<int>(blockIdx.x);
+  const int tstep = PAIR ? static_cast<int>(ptx::num_clusters_x()) : static_cast<int>(gridDim.x);
+  auto pix_base = [&](int pt) { return pt * (PAIR ? 2 * kTileM : kTileM) + rank * kTileM; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       ptx::mbar_init(full_a + 8 * s, kNumSampWarps);
       ptx::mbar_init(full_b + 8 * s, 1);
       ptx::mbar_init(empty + 8 * s, 1);
+      ptx::mbar_init(full_peer + 8 * s, 1);
     }
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(tfull + 8 * i, 1);
-      ptx::mbar_init(tempty + 8 * i, kNumEpiWarps);
+      ptx::mbar_init(tempty + 8 * i, PAIR ? 2 * kNumEpiWarps : kNumEpiWarps);
     }
     ptx::mbar_init(drain, 1);
     for (int i = 0; i < 2; ++i) {
@@ -319,11 +431,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::fence_mbar_init();
   }
   if (warp == kMmaWarp) {
-    ptx::tmem_alloc(ptx::smem_addr(tmem_slot), args.tmem_cols);
-    ptx::tmem_relinquish();
+    if (PAIR) {
+      ptx::tmem_alloc_pair(ptx::smem_addr(tmem_slot), args.tmem_cols);
+      ptx::tmem_relinquish_pair();
+    } else {
+      ptx::tmem_alloc(ptx::smem_addr(tmem_slot), args.tmem_cols);
+      ptx::tmem_relinquish();
+    }
   }
   ptx::tc_fence_before();
-  __syncthreads();
+  if (PAIR) ptx::cluster_sync();  // barriers of both CTAs initialised before any remote arrive
+  else __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -334,19 +452,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ph = 0;
       bool ok = true;
       const uint32_t b_base = ptx::smem_addr(b_smem);
-      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
+      // a K-block of packed weights holds both halves of a pair, this CTA copies its own
+      const size_t kb_bytes = static_cast<size_t>(args.b_stage_bytes) * (PAIR ? 2 : 1);
+      for (int tile = tile0; tile < args.num_tiles && ok; tile += tstep) {
         int img, pt, cc;
         decode_tile(args, tile, img, pt, cc);
-        const uint8_t* src = args.wpack + static_cast<size_t>(cc) * args.numKB * args.b_stage_bytes;
+        const uint8_t* src = args.wpack + static_cast<size_t>(cc) * args.numKB * kb_bytes +
+                             static_cast<size_t>(rank) * args.b_stage_bytes;
         for (int kb = 0; kb < args.numKB; ++kb, ++it) {
-          if (!wait_bar<kSuspend>(empty + 8 * s, ph ^ 1, args, abort_flag,
+          if (!wait_bar<kSuspend>(empty + 8 * s, ph ^ 1, wc,
                                   DCNV2_DEVERR_TIMEOUT_PRODUCER)) {
             ok = false;
             break;
           }
           ptx::mbar_arrive_expect_tx(full_b + 8 * s, args.b_stage_bytes);
           ptx::bulk_copy_g2s(b_base + s * args.b_stage_bytes,
-                             src + static_cast<size_t>(kb) * args.b_stage_bytes,
+                             src + static_cast<size_t>(kb) * kb_bytes,
                              args.b_stage_bytes, full_b + 8 * s);
           if (++s == S) { s = 0; ph ^= 1u; }
         }
@@ -356,90 +477,68 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int outstanding = it < S ? it : S;
       for (int j = 0; j < outstanding; ++j) {
         const int idx = it - 1 - j;
-        wait_bar(full_b + 8 * (idx % S), (idx / S) & 1, args, abort_flag, DCNV2_DEVERR_TIMEOUT_DRAIN);
+        wait_bar(full_b + 8 * (idx % S), (idx / S) & 1, wc, DCNV2_DEVERR_TIMEOUT_DRAIN);
       }
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    // A single thread on the critical path: it spins (the samplers suspend), keeps stage and
-    // phase counters incrementally and only patches the start-address field of the descriptors.
-    if (lane == 0) {
-      uint32_t idesc;
-      if (PREC == PREC_F16) idesc = ptx::make_idesc(1, 0, args.n_mma);
-      else if (PREC == PREC_I8) idesc = ptx::make_idesc(2, 1, args.n_mma);
-      else idesc = ptx::make_idesc(1, 2, args.n_mma);
-      const uint64_t desc0 = ptx::sw128_kmajor_desc(0);  // every field but the address
-      const uint32_t a_base = ptx::smem_addr(a_smem);
-      const uint32_t b_base = ptx::smem_addr(b_smem);
-      const uint32_t acc_cols = static_cast<uint32_t>(args.nrows);
-      const uint32_t sub_bytes = static_cast<uint32_t>(args.n_mma) * kRowBytes;
-      const uint32_t lo_bytes = static_cast<uint32_t>(args.nrows) * kRowBytes;
-      const int nsub = args.nsub, numKB = args.numKB;
-      int s = 0, acc = 0;
-      uint32_t ph = 0, use = 0;
+    if (lane == 0 && (!PAIR || rank == 0)) {
+      MmaParams mp;
+      mp.a_base = ptx::smem_addr(a_smem);
+      mp.b_base = ptx::smem_addr(b_smem);
+      mp.a_stage_bytes = args.a_stage_bytes;
+      mp.b_stage_bytes = args.b_stage_bytes;
+      mp.tmem_base = tmem_base;
+      mp.full_a = full_a; mp.full_b = full_b; mp.full_peer = full_peer; mp.empty = empty;
+      mp.tfull = tfull; mp.tempty = tempty; mp.drain = drain;
+      mp.S = S; mp.num_tiles = args.num_tiles; mp.tile0 = tile0; mp.tstep = tstep;
+      mp.numKB = args.numKB; mp.n_mma = args.n_mma; mp.nrows = args.nrows;
+      mp.acc_bufs = args.acc_bufs;
+      mp.wc = wc;
+      // nsub is 1 or 2 (at most 512 output channels per tile)
+      if (args.nsub == 1) {
+        if (PREC == PREC_F32 && args.tf32_single) mma_issuer<PREC, PAIR, 1, true>(mp);
+        else mma_issuer<PREC, PAIR, 1, false>(mp);
+      } else {
+        if (PREC == PREC_F32 && args.tf32_single) mma_issuer<PREC, PAIR, 2, true>(mp);
+        else mma_issuer<PREC, PAIR, 2, false>(mp);
+      }
+    } else if (PAIR && lane == 0) {
+      // Rank 1 relay: once this CTA's A and B of a stage have landed, tell the leader.
+      const uint32_t peer_full = ptx::mapa_shared(full_peer, 0);
+      int s = 0;
+      uint32_t ph = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
-        if (!wait_bar<64>(tempty + 8 * acc, use ^ 1, args, abort_flag, DCNV2_DEVERR_TIMEOUT_MMA)) {
-          ok = false;
-          break;
-        }
-        ptx::tc_fence_after();
-        const uint32_t d_base = tmem_base + acc * acc_cols;
-        for (int kb = 0; kb < numKB; ++kb) {
-          if (!wait_bar(full_a + 8 * s, ph, args, abort_flag, DCNV2_DEVERR_TIMEOUT_MMA) ||
-              !wait_bar(full_b + 8 * s, ph, args, abort_flag, DCNV2_DEVERR_TIMEOUT_MMA)) {
+      for (int tile = tile0; tile < args.num_tiles && ok; tile += tstep) {
+        for (int kb = 0; kb < args.numKB; ++kb) {
+          if (!wait_bar(full_a + 8 * s, ph, wc, DCNV2_DEVERR_TIMEOUT_MMA) ||
+              !wait_bar(full_b + 8 * s, ph, wc, DCNV2_DEVERR_TIMEOUT_MMA)) {
             ok = false;
             break;
           }
-          ptx::tc_fence_after();
-          const uint64_t ad0 = desc0 | (((a_base + s * args.a_stage_bytes) >> 4) & 0x3FFFu);
-          const uint64_t bd0 = desc0 | (((b_base + s * args.b_stage_bytes) >> 4) & 0x3FFFu);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint64_t ad = ad0 + 2 * k;  // +32 bytes per K-step (address field in 16 B)
-            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
-            for (int sub = 0; sub < nsub; ++sub) {
-              const uint32_t d = d_base + sub * args.n_mma;
-              const uint64_t bd = bd0 + 2 * k + ((sub * sub_bytes) >> 4);
-              if (PREC == PREC_F16) {
-                ptx::mma_f16(d, ad, bd, idesc, accum);
-              } else if (PREC == PREC_I8) {
-                ptx::mma_i8(d, ad, bd, idesc, accum);
-              } else {
-                ptx::mma_tf32(d, ad, bd, idesc, accum);
-                if (!args.tf32_single) {
-                  ptx::mma_tf32(d, ad, bd + (lo_bytes >> 4), idesc, 1u);
-                  ptx::mma_tf32(d, ad + (kATileBytes >> 4), bd, idesc, 1u);
-                }
-              }
-            }
-          }
-          ptx::tc_commit(empty + 8 * s);  // frees this stage once its MMAs have read it
+          ptx::mbar_arrive_cluster(peer_full + 8 * s);
           if (++s == S) { s = 0; ph ^= 1u; }
         }
-        if (!ok) break;
-        ptx::tc_commit(tfull + 8 * acc);  // accumulator ready for the epilogue
-        if (++acc == args.acc_bufs) { acc = 0; use ^= 1u; }
       }
-      ptx::tc_commit(drain);
-      wait_bar(drain, 0, args, abort_flag, DCNV2_DEVERR_TIMEOUT_DRAIN);
+      // the leader's last commit: every MMA reading this CTA's memory or TMEM has completed
+      wait_bar(drain, 0, wc, DCNV2_DEVERR_TIMEOUT_DRAIN);
     }
   } else if (warp < kSampWarp0) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const uint32_t acc_cols = static_cast<uint32_t>(args.nrows);
     int tl = 0;
-    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++tl) {
+    for (int tile = tile0; tile < args.num_tiles; tile += tstep, ++tl) {
       const int acc = tl % args.acc_bufs;
       const uint32_t ph = (tl / args.acc_bufs) & 1;
       // Warp-uniform outcome: every lane must take part in the tcgen05.ld below or none.
       const bool got =
-          wait_bar<256>(tfull + 8 * acc, ph, args, abort_flag, DCNV2_DEVERR_TIMEOUT_EPILOGUE);
+          wait_bar<256>(tfull + 8 * acc, ph, wc, DCNV2_DEVERR_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, got)) break;
       ptx::tc_fence_after();
       int img, pt, cc;
       decode_tile(args, tile, img, pt, cc);
-      const int p = pt * kTileM + q * 32 + lane;
+      const int p = pix_base(pt) + q * 32 + lane;
       const bool pvalid = p < args.P;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * acc_cols;
       const int o_chunk = cc * args.nrows;
@@ -477,7 +576,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(tempty + 8 * acc);
+      if (lane == 0) {
+        if (PAIR && rank != 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(tempty + 8 * acc, 0));
+        else ptx::mbar_arrive(tempty + 8 * acc);
+      }
     }
   } else {
     // ------------------------------------------------------------ samplers
@@ -530,15 +632,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // q & 1 is released by all sampler warps (its use q - 2), then one 4-D TMA box.
     auto issue_window = [&](int q) -> bool {
       const int k = q / cb_per_tile, r = q - k * cb_per_tile;
-      const int tl = blockIdx.x + k * gridDim.x;
+      const int tl = tile0 + k * tstep;
       if (tl >= args.num_tiles) return true;
       const int g = r / args.CBg, cbg = r - g * args.CBg;
       int im, pt, cc;
       decode_tile(args, tl, im, pt, cc);
-      const int row0 = ((pt * kTileM) / args.Wo) * args.stride - args.win_top;
+      const int row0 = (pix_base(pt) / args.Wo) * args.stride - args.win_top;
       const int b = q & 1;
       const uint32_t use = static_cast<uint32_t>(q >> 1) & 1u;
-      if (!wait_bar<kSuspend>(win_empty + 8 * b, use ^ 1u, args, abort_flag, DCNV2_DEVERR_TIMEOUT_SAMPLER))
+      if (!wait_bar<kSuspend>(win_empty + 8 * b, use ^ 1u, wc, DCNV2_DEVERR_TIMEOUT_SAMPLER))
         return false;
       ptx::mbar_arrive_expect_tx(win_full + 8 * b, args.win_bytes);
       ptx::tma_load_4d(w_base + b * args.win_bytes, &tmap_x, (g * args.Cg + cbg * KC) * EB, 0,
@@ -549,29 +651,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (issuer) ok = issue_window(0) && issue_window(1);
     ok = __all_sync(0xffffffffu, ok);
 
-    for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
+    // L2 prefetch of the offsets and mask of tile `tl` (this CTA's pixels, every group): the
+    // items of a tile are computed from them when it starts, one tile after the prefetch. Every
+    // address lies inside the prefetched range.
+    auto prefetch_geometry = [&](int tl) {
+      if (tl >= args.num_tiles) return;
+      int im, ptn, ccn;
+      decode_tile(args, tl, im, ptn, ccn);
+      const int p0 = pix_base(ptn);
+      const int cnt = args.P - p0 < kTileM ? args.P - p0 : kTileM;
+      if (cnt <= 0) return;
+      const int bytes = cnt * static_cast<int>(sizeof(GT));
+      const int lines = (bytes + 127) / 128 + 1;  // +1: the range may straddle one more line
+      const int off_planes = 2 * args.T * args.dg;
+      const int planes = off_planes + args.T * args.dg;
+      for (int i = lane; i < planes * lines; i += 32) {
+        const int pl = i / lines, ln = i - pl * lines;
+        const GT* base = pl < off_planes
+                             ? offp + (static_cast<size_t>(im) * off_planes + pl) * args.P + p0
+                             : maskp + (static_cast<size_t>(im) * args.T * args.dg +
+                                        (pl - off_planes)) * args.P + p0;
+        const int at = ln * 128 < bytes - 1 ? ln * 128 : bytes - 1;
+        ptx::prefetch_l2(reinterpret_cast<const uint8_t*>(base) + at);
+      }
+    };
+
+    for (int tile = tile0; tile < args.num_tiles && ok; tile += tstep) {
       int img, pt, cc;
       decode_tile(args, tile, img, pt, cc);
-      const int my_pix = pt * kTileM + ps + kSampRowStride * myr;
+      const int my_pix = pix_base(pt) + ps + kSampRowStride * myr;
       const bool my_val = my_pix < args.P;
       const int pcl = my_val ? my_pix : 0;
       const int oh = pcl / args.Wo, ow = pcl - (pcl / args.Wo) * args.Wo;
       const int my_bh = oh * args.stride - args.pad;
       const int my_bw = ow * args.stride - args.pad;
-      const int row0 = ((pt * kTileM) / args.Wo) * args.stride - args.win_top;
+      const int row0 = (pix_base(pt) / args.Wo) * args.stride - args.win_top;
       const uint8_t* ximg = args.x_nhwc + static_cast<size_t>(img) * args.H * args.W * args.C * EB;
+      if (sw == 0) prefetch_geometry(tile + tstep);
 
       // this lane's item of tap t: weight word (packed for the fp16 fast path) and global pixel
-      auto item = [&](int g, int t, uint32_t& wword, int& gpix) {
+      // geometry value i of (group g) for this lane's pixel: i = 3t + {0: dh, 1: dw, 2: mask}
+      auto geom = [&](int g, int i) -> float {
+        const int t = i / 3, comp = i - 3 * t;
+        const size_t ig = static_cast<size_t>(img) * args.dg + g;
+        return comp < 2 ? load_geom_value(offp + (ig * 2 * args.T + 2 * t + comp) * args.P + my_pix)
+                        : load_geom_value(maskp + (ig * args.T + t) * args.P + my_pix);
+      };
+      // this lane's item of tap t from the pixel's (dh, dw, m)
+      auto item_from = [&](int t, float dh, float dw, float m, uint32_t& wword, int& gpix) {
         const int ki = t / args.K, kj = t - ki * args.K;
-        float dh = 0.f, dw = 0.f, m = 0.f;
-        if (my_val) {
-          const size_t goff = (static_cast<size_t>(img) * args.dg + g) * 2 * args.T + 2 * t;
-          const size_t gmsk = (static_cast<size_t>(img) * args.dg + g) * args.T + t;
-          dh = load_geom_value(offp + goff * args.P + my_pix);
-          dw = load_geom_value(offp + (goff + 1) * args.P + my_pix);
-          m = load_geom_value(maskp + gmsk * args.P + my_pix);
-        }
         const float hf = __fadd_rn(static_cast<float>(my_bh + ki * args.dil), dh);
         const float wf = __fadd_rn(static_cast<float>(my_bw + kj * args.dil), dw);
         const bool inside = my_val && !(hf <= -1.f || hf >= static_cast<float>(args.H) ||
@@ -601,6 +729,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           gpix = (wpix != kNoWin) ? -static_cast<int>(wpix) - 1 : gpix;  // < 0: window pixel
         }
       };
+      auto item = [&](int g, int t, uint32_t& wword, int& gpix) {
+        float dh = 0.f, dw = 0.f, m = 0.f;
+        if (my_val) {
+          dh = geom(g, 3 * t);
+          dw = geom(g, 3 * t + 1);
+          m = geom(g, 3 * t + 2);
+        }
+        item_from(t, dh, dw, m, wword, gpix);
+      };
 
       for (int g = 0; g < args.dg && ok; ++g) {
         // items of every tap, computed once per (tile, group) for 3x3 kernels
@@ -608,10 +745,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         int cg[kCache];
         bool fast_g = false;
         if (KT > 0) {
+          // The 4 lanes of a (pixel, row) share its 3*KT geometry values: lane c loads values
+          // c, c+4, c+8, ... (one round trip of independent loads) and the rest are shuffled in.
+          constexpr int kGeo = 3 * kCache, kPer = (kGeo + 3) / 4;
+          float gv[kPer];
+#pragma unroll
+          for (int q = 0; q < kPer; ++q) {
+            const int i = 4 * q + myc;
+            gv[q] = (my_val && i < kGeo) ? geom(g, i) : 0.f;
+          }
+          const int gl = lane & ~3;
           bool inwin = true;
 #pragma unroll
           for (int t = 0; t < kCache; ++t) {
-            item(g, t, cw[t], cg[t]);
+            const float dh = __shfl_sync(0xffffffffu, gv[(3 * t) >> 2], gl | ((3 * t) & 3));
+            const float dw = __shfl_sync(0xffffffffu, gv[(3 * t + 1) >> 2], gl | ((3 * t + 1) & 3));
+            const float m = __shfl_sync(0xffffffffu, gv[(3 * t + 2) >> 2], gl | ((3 * t + 2) & 3));
+            item_from(t, dh, dw, m, cw[t], cg[t]);
             inwin = inwin && ((cw[t] >> 16) != kNoWin);
           }
           fast_g = kPacked && __all_sync(0xffffffffu, inwin);
@@ -621,7 +771,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int b = cbi & 1;
           if (args.use_win) {
             const bool got = wait_bar<kSuspend>(win_full + 8 * b, static_cast<uint32_t>(cbi >> 1) & 1u,
-                                      args, abort_flag, DCNV2_DEVERR_TIMEOUT_SAMPLER);
+                                      wc, DCNV2_DEVERR_TIMEOUT_SAMPLER);
             if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
           }
           const uint32_t win = w_base + b * args.win_bytes + j * 16;
@@ -631,36 +781,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint8_t* gsrc = ximg + static_cast<size_t>(gbase + cig) * EB;
           if (kPacked && fast_g && all_valid) {
             // Fast path: every corner of every tap of this warp is in the window and every
-            // chunk is full. Straight-line per tap: 8 shuffles, 8 shared loads, mix, 2 stores.
+            // chunk is full. Straight-line per tap: 8 shuffles, 8 shared loads and the mix run
+            // before the stage is free; only the 2 stores and the arrive follow the wait (the
+            // stage hand-off is the latency-critical loop of the pipeline).
 #pragma unroll
             for (int tt = 0; tt < kCache; ++tt) {
-              uint32_t wv[R][4];
-              uint4 xv[R][4];
+              uint4 out[R];
 #pragma unroll
-              for (int r = 0; r < R; ++r)
+              for (int r = 0; r < R; ++r) {
+                uint32_t wv[4];
+                uint4 xv[4];
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                   const uint32_t v = __shfl_sync(0xffffffffu, cw[tt], grp | (r * 4 + c));
-                  wv[r][c] = v;                                   // fp16 weight in bits 0-15
-                  xv[r][c] = ptx::ld_shared_v4(win + (v >> 16));  // window byte offset
+                  wv[c] = v;                                   // fp16 weight in bits 0-15
+                  xv[c] = ptx::ld_shared_v4(win + (v >> 16));  // window byte offset
                 }
+                const __half2 w0 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[0])));
+                const __half2 w1 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[1])));
+                const __half2 w2 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[2])));
+                const __half2 w3 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[3])));
+                out[r].x = f16_mix_h2(w0, w1, w2, w3, xv[0].x, xv[1].x, xv[2].x, xv[3].x);
+                out[r].y = f16_mix_h2(w0, w1, w2, w3, xv[0].y, xv[1].y, xv[2].y, xv[3].y);
+                out[r].z = f16_mix_h2(w0, w1, w2, w3, xv[0].z, xv[1].z, xv[2].z, xv[3].z);
+                out[r].w = f16_mix_h2(w0, w1, w2, w3, xv[0].w, xv[1].w, xv[2].w, xv[3].w);
+              }
               const bool got =
-                  wait_bar<kSuspend>(empty + 8 * s, ph ^ 1, args, abort_flag, DCNV2_DEVERR_TIMEOUT_SAMPLER);
+                  wait_bar<kSuspend>(empty + 8 * s, ph ^ 1, wc, DCNV2_DEVERR_TIMEOUT_SAMPLER);
               if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
               const uint32_t a_s = a_base + s * args.a_stage_bytes;
 #pragma unroll
-              for (int r = 0; r < R; ++r) {
-                const __half2 w0 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[r][0])));
-                const __half2 w1 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[r][1])));
-                const __half2 w2 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[r][2])));
-                const __half2 w3 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[r][3])));
-                uint4 out;
-                out.x = f16_mix_h2(w0, w1, w2, w3, xv[r][0].x, xv[r][1].x, xv[r][2].x, xv[r][3].x);
-                out.y = f16_mix_h2(w0, w1, w2, w3, xv[r][0].y, xv[r][1].y, xv[r][2].y, xv[r][3].y);
-                out.z = f16_mix_h2(w0, w1, w2, w3, xv[r][0].z, xv[r][1].z, xv[r][2].z, xv[r][3].z);
-                out.w = f16_mix_h2(w0, w1, w2, w3, xv[r][0].w, xv[r][1].w, xv[r][2].w, xv[r][3].w);
-                ptx::st_shared_v4(a_s + dst_off[r], out);
-              }
+              for (int r = 0; r < R; ++r) ptx::st_shared_v4(a_s + dst_off[r], out[r]);
               ptx::fence_proxy_async_smem();
               __syncwarp();
               if (lane == 0) ptx::mbar_arrive(full_a + 8 * s);
@@ -690,10 +841,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     loc[r][c] = gp < 0 ? (-gp - 1) * kRowBytes : -gp - 1;
                   }
                 }
-              const bool got =
-                  wait_bar<kSuspend>(empty + 8 * s, ph ^ 1, args, abort_flag, DCNV2_DEVERR_TIMEOUT_SAMPLER);
-              if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
-              const uint32_t a_s = a_base + s * args.a_stage_bytes;
+              // loads and mix before the stage is free; stores after
+              uint4 outs[R], outs_lo[R];
 #pragma unroll
               for (int r = 0; r < R; ++r) {
                 uint4 xv[4];
@@ -741,8 +890,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                   }
                 }
-                ptx::st_shared_v4(a_s + dst_off[r], out);
-                if (PREC == PREC_F32) ptx::st_shared_v4(a_s + dst_off[r] + kATileBytes, out_lo);
+                outs[r] = out;
+                outs_lo[r] = out_lo;
+              }
+              const bool got =
+                  wait_bar<kSuspend>(empty + 8 * s, ph ^ 1, wc, DCNV2_DEVERR_TIMEOUT_SAMPLER);
+              if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+              const uint32_t a_s = a_base + s * args.a_stage_bytes;
+#pragma unroll
+              for (int r = 0; r < R; ++r) {
+                ptx::st_shared_v4(a_s + dst_off[r], outs[r]);
+                if (PREC == PREC_F32) ptx::st_shared_v4(a_s + dst_off[r] + kATileBytes, outs_lo[r]);
               }
               ptx::fence_proxy_async_smem();
               __syncwarp();
@@ -765,17 +923,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Window loads still in flight (only after an abort) must land before the CTA exits.
     if (issuer) {
       for (int q = issued - 2 < 0 ? 0 : issued - 2; q < issued; ++q)
-        wait_bar(win_full + 8 * (q & 1), static_cast<uint32_t>(q >> 1) & 1u, args, abort_flag,
+        wait_bar(win_full + 8 * (q & 1), static_cast<uint32_t>(q >> 1) & 1u, wc,
                  DCNV2_DEVERR_TIMEOUT_DRAIN);
     }
   }
 
   ptx::tc_fence_before();
-  __syncthreads();
+  // A pair stays resident until both CTAs are done: the leader's MMAs read rank 1's shared memory
+  // and rank 1's epilogue arrives on the leader's barriers.
+  if (PAIR) ptx::cluster_sync();
+  else __syncthreads();
   if (warp == kMmaWarp) {
     __syncwarp();  // lane 0 ran the MMA loop alone; reconverge for the .sync.aligned dealloc
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, args.tmem_cols);
+    if (PAIR) ptx::tmem_dealloc_pair(tmem_base, args.tmem_cols);
+    else ptx::tmem_dealloc(tmem_base, args.tmem_cols);
   }
 }
 
@@ -845,7 +1007,7 @@ __global__ void __launch_bounds__(256) pack_weights_kernel(const void* __restric
                                                            uint8_t* __restrict__ wpack,
                                                            int* err, int O, int C, int T,
                                                            int Cg, int CBg, int numKB,
-                                                           int nrows, int cchunks) {
+                                                           int nrows, int cchunks, int half_mma) {
   using TR = PrecTraits<PREC>;
   constexpr int EPC = TR::kChunkElems, KC = TR::kBlockElems;
   if (blockIdx.x == 0 && threadIdx.x == 0) *err = 0;
@@ -862,7 +1024,16 @@ __global__ void __launch_bounds__(256) pack_weights_kernel(const void* __restric
     const int g = kb / (CBg * T);
     const int o = cc * nrows + row;
     const size_t tile_base = blk * TR::kNumBTiles * nrows * kRowBytes;
-    const size_t dst = tile_base + static_cast<size_t>(row) * kRowBytes + ((jc ^ (row & 7)) << 4);
+    // CTA pair (half_mma = n_mma / 2 > 0): rows [sub*n_mma + rk*half_mma, +half_mma) go to CTA
+    // rk's half of the K-block, sub-MMA blocks consecutive. half_mma is a multiple of 8, so the
+    // swizzle phase (row % 8) is unchanged.
+    int srow = row;
+    if (half_mma > 0) {
+      const int sub = row / (2 * half_mma), r = row - sub * 2 * half_mma;
+      const int rk = r / half_mma;
+      srow = rk * (nrows / 2) + sub * half_mma + (r - rk * half_mma);
+    }
+    const size_t dst = tile_base + static_cast<size_t>(srow) * kRowBytes + ((jc ^ (srow & 7)) << 4);
     uint4 hi = make_uint4(0, 0, 0, 0), lo = make_uint4(0, 0, 0, 0);
     uint8_t* hb = reinterpret_cast<uint8_t*>(&hi);
     uint8_t* lb = reinterpret_cast<uint8_t*>(&lo);

@@ -284,3 +284,36 @@ def test_timeout_selftest_keeps_context_usable():
     assert st == Status.ERR_DEVICE_TIMEOUT and code != 0
     fx = load("kat_16c_32.npz")
     assert np.abs(run_fp32(fx) - fx["y"]).max() <= FP32_TOL
+
+
+PAIR_SHAPES = {
+    # P = 33*29 = 957 (not a multiple of 256: the last pair tile's second CTA has no pixels)
+    "c32_o24_s2": dict(n=3, c=32, o=24, h=33, w=29, s=2),
+    "c128_o512_dg8_d2": dict(n=1, c=128, o=512, h=24, w=24, p=2, d=2, dg=8, ostd=2.0),
+    "c256_o256_oob": dict(n=1, c=256, o=256, h=32, w=48, ostd=0.5, outl=0.05),
+    "c64_o48_hw40": dict(n=2, c=64, o=48, h=40, w=40),
+}
+
+
+@pytest.mark.parametrize("shape", sorted(PAIR_SHAPES))
+def test_cta_pair_and_single_cta_paths_agree(shape, monkeypatch):
+    """fp16 / int8 run one CTA per 128-pixel tile by default; DCNV2_PAIR=1 selects CTA pairs
+    (cta_group::2, 256-pixel tiles). Both meet the stated bounds and agree with each other."""
+    fx = random_case(**PAIR_SHAPES[shape])
+    h = half_inputs(fx)
+    ref16 = oracle.forward_ref(h["x"], h["offset"], h["mask"], h["weight"], h["bias"],
+                               *oattrs(fx), precision="fp16")
+    xq, xs, wq, ws = quantized(fx)
+    monkeypatch.setenv("DCNV2_PAIR", "1")
+    y16_pair = run_fp16(fx)
+    y8_pair = run_int8(fx, xq, xs, wq, ws)
+    monkeypatch.delenv("DCNV2_PAIR")
+    y16_one = run_fp16(fx)
+    y8_one = run_int8(fx, xq, xs, wq, ws)
+    for y in (y16_pair, y16_one):
+        assert mean_rel(y, ref16) <= FP16_MEAN_REL
+    for y in (y8_pair, y8_one):
+        check_int8(fx, y, xq, xs, wq, ws)
+    # same A and B operands and K order: the two paths differ at most by fp32 accumulation order
+    assert mean_rel(y16_pair, y16_one) <= 1e-4
+    np.testing.assert_allclose(y8_pair, y8_one, rtol=1e-6, atol=1e-6)
