@@ -762,9 +762,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float dw = __shfl_sync(0xffffffffu, gv[(3 * t + 1) >> 2], gl | ((3 * t + 1) & 3));
             const float m = __shfl_sync(0xffffffffu, gv[(3 * t + 2) >> 2], gl | ((3 * t + 2) & 3));
             item_from(t, dh, dw, m, cw[t], cg[t]);
-            inwin = inwin && ((cw[t] >> 16) != kNoWin);
+            // in the window: packed word's high half, else a negative (window) location
+            inwin = inwin && (kPacked ? ((cw[t] >> 16) != kNoWin) : (cg[t] < 0));
           }
-          fast_g = kPacked && __all_sync(0xffffffffu, inwin);
+          // fp32 keeps the general path (two A tiles per K-block)
+          fast_g = PREC != PREC_F32 && __all_sync(0xffffffffu, inwin);
         }
         const int gbase = g * args.Cg;
         for (int cbg = 0; cbg < args.CBg && ok; ++cbg) {
@@ -805,6 +807,46 @@ __global__ void __launch_bounds__(kThreads, 1)
                 out[r].y = f16_mix_h2(w0, w1, w2, w3, xv[0].y, xv[1].y, xv[2].y, xv[3].y);
                 out[r].z = f16_mix_h2(w0, w1, w2, w3, xv[0].z, xv[1].z, xv[2].z, xv[3].z);
                 out[r].w = f16_mix_h2(w0, w1, w2, w3, xv[0].w, xv[1].w, xv[2].w, xv[3].w);
+              }
+              const bool got =
+                  wait_bar<kSuspend>(empty + 8 * s, ph ^ 1, wc, DCNV2_DEVERR_TIMEOUT_SAMPLER);
+              if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+              const uint32_t a_s = a_base + s * args.a_stage_bytes;
+#pragma unroll
+              for (int r = 0; r < R; ++r) ptx::st_shared_v4(a_s + dst_off[r], out[r]);
+              ptx::fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) ptx::mbar_arrive(full_a + 8 * s);
+              if (++s == S) { s = 0; ph ^= 1u; }
+            }
+          } else if (!kPacked && PREC != PREC_F32 && fast_g && all_valid) {
+            // Fast path of int8 and precise fp16: as above, with fp32 corner weights and window
+            // byte offsets shuffled separately (same arithmetic as the general path).
+#pragma unroll
+            for (int tt = 0; tt < kCache; ++tt) {
+              uint4 out[R];
+#pragma unroll
+              for (int r = 0; r < R; ++r) {
+                float wf4[4];
+                uint4 xv[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  const int src = grp | (r * 4 + c);
+                  wf4[c] = __uint_as_float(__shfl_sync(0xffffffffu, cw[tt], src));
+                  const int loc = __shfl_sync(0xffffffffu, cg[tt], src);  // -(window pixel) - 1
+                  xv[c] = ptx::ld_shared_v4(win + static_cast<uint32_t>(-loc - 1) * kRowBytes);
+                }
+                if (PREC == PREC_I8) {
+                  out[r].x = i8_mix_word(wf4, xv[0].x, xv[1].x, xv[2].x, xv[3].x);
+                  out[r].y = i8_mix_word(wf4, xv[0].y, xv[1].y, xv[2].y, xv[3].y);
+                  out[r].z = i8_mix_word(wf4, xv[0].z, xv[1].z, xv[2].z, xv[3].z);
+                  out[r].w = i8_mix_word(wf4, xv[0].w, xv[1].w, xv[2].w, xv[3].w);
+                } else {
+                  out[r].x = f16_mix_precise(wf4, xv[0].x, xv[1].x, xv[2].x, xv[3].x);
+                  out[r].y = f16_mix_precise(wf4, xv[0].y, xv[1].y, xv[2].y, xv[3].y);
+                  out[r].z = f16_mix_precise(wf4, xv[0].z, xv[1].z, xv[2].z, xv[3].z);
+                  out[r].w = f16_mix_precise(wf4, xv[0].w, xv[1].w, xv[2].w, xv[3].w);
+                }
               }
               const bool got =
                   wait_bar<kSuspend>(empty + 8 * s, ph ^ 1, wc, DCNV2_DEVERR_TIMEOUT_SAMPLER);
