@@ -19,6 +19,7 @@
 #include "../../include/dcnv2_diag.h"
 #include <cudaTypedefs.h>
 #include "dcnv2_kernels.cuh"
+#include "dcnv2_ta_kernel.cuh"
 
 namespace dcnv2 {
 
@@ -109,6 +110,10 @@ struct Plan {
   int win_rows = 0, win_top = 0;
   uint32_t win_bytes = 0;
   bool tf32_single = false, precise = false;
+  // A operand in TMEM (dcnv2_fused_ta_kernel): A ring in TMEM, B ring in shared memory
+  bool ta = false;
+  int a_stages = 0, b_stages = 0;
+  uint32_t win_stride = 0;
 };
 
 int prec_of(int dtype) {
@@ -123,6 +128,85 @@ int prec_of(int dtype) {
 int elem_bytes_of(int prec) { return prec == PREC_F32 ? 4 : prec == PREC_F16 ? 2 : 1; }
 int chunk_elems_of(int prec) { return prec == PREC_F32 ? 4 : prec == PREC_F16 ? 8 : 16; }
 int block_elems_of(int prec) { return prec == PREC_F32 ? 32 : prec == PREC_F16 ? 64 : 128; }
+
+// Largest number of output rows of a tile of `tile_px` consecutive output pixels (whole image
+// scan for up to 4096 tiles; beyond that with Wo > 4096 no exact bound is taken).
+int max_tile_rows(const Plan& p, int tile_px) {
+  const int64_t P = int64_t(p.Ho) * p.Wo;
+  const int64_t tiles = (P + tile_px - 1) / tile_px;
+  int rows_max = 0;
+  const int64_t loop = tiles < 4096 ? tiles : 4096;
+  for (int64_t pt = 0; pt < loop; ++pt) {
+    const int64_t a0 = pt * tile_px, a1 = (a0 + tile_px < P ? a0 + tile_px : P) - 1;
+    const int rows = static_cast<int>(a1 / p.Wo - a0 / p.Wo + 1);
+    if (rows > rows_max) rows_max = rows;
+  }
+  if (tiles > 4096 && p.Wo > 4096) rows_max = 1 << 20;
+  return rows_max;
+}
+
+// Configuration of dcnv2_fused_ta_kernel: one accumulator of n_mma <= 256 columns and up to 8
+// A stages of 32 columns in 512 TMEM columns; shared memory holds two x windows (1 KB aligned,
+// 128-byte swizzle) and the B ring. The window covers, for every pixel of a CTA's 128, the taps
+// whose offsets lie in (-1 - M, 1 + M) for the largest margin M <= 2 that still leaves three B
+// stages (else two); corners outside it are read from global memory.
+void plan_ta(Plan* pl) {
+  Plan& p = *pl;
+  p.ta = true;
+  p.cchunks = static_cast<int>(cdiv(p.O, 256));
+  p.nsub = 1;
+  p.n_mma = static_cast<int>(cdiv(cdiv(p.O, p.cchunks), 16) * 16);
+  p.nrows = p.n_mma;
+  p.acc_bufs = 1;
+  p.tmem_cols = kTaTmemCols;
+  p.a_stages = kTaMaxAStages;
+  p.a_stage_bytes = 0;
+  p.b_kb_bytes = size_t(p.nrows) * kRowBytes;
+  p.b_stage_bytes = static_cast<uint32_t>(p.b_kb_bytes / (p.pair ? 2 : 1));
+  const int64_t cta_tiles_per_img = cdiv(int64_t(p.Ho) * p.Wo, kTileM);
+  p.tiles_per_img = static_cast<int>(p.pair ? cdiv(int64_t(p.Ho) * p.Wo, 2 * kTileM)
+                                            : cta_tiles_per_img);
+  p.num_tiles = static_cast<int>(int64_t(p.N) * p.tiles_per_img * p.cchunks);
+  const size_t fixed = 1024 + 512;
+  const size_t per_stage = p.b_stage_bytes;
+  auto b_stages_for = [&](size_t win_total) {
+    int sb = static_cast<int>((kSmemLimit - fixed - win_total) / per_stage);
+    return sb > kTaMaxBStages ? kTaMaxBStages : sb;
+  };
+  p.use_win = false;
+  p.win_rows = 0; p.win_top = 0; p.win_bytes = 0; p.win_stride = 0;
+  p.b_stages = b_stages_for(0);
+  if (p.W <= 256) {
+    const int rows_max = max_tile_rows(p, kTileM);
+    const int64_t base = int64_t(rows_max - 1) * p.stride + int64_t(p.K - 1) * p.dil + 3;
+    bool done = false;
+    for (int want = 3; want >= 2 && !done; --want) {
+      for (int M = 2; M >= 0; --M) {
+        const int64_t rows = base + 2 * M;
+        if (rows > 256) continue;
+        const size_t wb = size_t(rows) * p.W * kRowBytes;
+        if (wb > 65536) continue;  // window byte offsets travel in 16 bits
+        const size_t stride = align_up(wb, 1024);
+        if (2 * stride + fixed + size_t(want) * per_stage > kSmemLimit) continue;
+        p.use_win = true;
+        p.win_rows = static_cast<int>(rows);
+        p.win_top = p.pad + 1 + M;
+        p.win_bytes = static_cast<uint32_t>(wb);
+        p.win_stride = static_cast<uint32_t>(stride);
+        p.b_stages = b_stages_for(2 * stride);
+        done = true;
+        break;
+      }
+    }
+  }
+  if (p.b_stages < 2) {
+    p.ta = false;  // not reached for nrows <= 256 (32 KB stages); the caller keeps its plan
+    return;
+  }
+  p.stages = p.b_stages;
+  p.smem_bytes = fixed + (p.use_win ? 2 * size_t(p.win_stride) : 0) +
+                 size_t(p.b_stages) * per_stage;
+}
 
 dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
   if (!d || !pl) return DCNV2_ERR_INVALID_ARG;
@@ -253,6 +337,19 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
       }
     }
   }
+  // fp16 / int8 with at most 256 output channels take the kernel with the A operand in TMEM
+  // (environment DCNV2_KERNEL=smem keeps the shared-memory A kernel; DCNV2_KERNEL=ta also uses
+  // it for wider layers, one output-channel chunk of <= 256 per tile).
+  if (p.fused && (prec == PREC_F16 || prec == PREC_I8)) {
+    const char* ke = std::getenv("DCNV2_KERNEL");
+    const bool force_smem = ke && std::strcmp(ke, "smem") == 0;
+    const bool force_ta = ke && std::strcmp(ke, "ta") == 0;
+    if (!force_smem && (p.O <= 256 || force_ta)) {
+      Plan t = p;
+      plan_ta(&t);
+      if (t.ta) p = t;
+    }
+  }
   // Workspace: [error word | x channels-last | packed weights]; +256 so that any base pointer
   // can be aligned up to 256 bytes.
   if (p.fused) p.kind = KIND_TCGEN05;
@@ -316,7 +413,16 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
       ok = ok && set_smem_attr(dcnv2_fused_kernel<PREC, true, 9, false>) &&
            set_smem_attr(dcnv2_fused_kernel<PREC, true, 0, false>) &&
            set_smem_attr(dcnv2_fused_kernel<PREC, true, 9, true>) &&
-           set_smem_attr(dcnv2_fused_kernel<PREC, true, 0, true>);
+           set_smem_attr(dcnv2_fused_kernel<PREC, true, 0, true>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 9, false>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 9, true>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, false>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, true>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, true, 0, false>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, true, 0, true>);
+    if constexpr (PREC == PREC_I8)
+      ok = ok && set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, false>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, true>);
     if (!ok) return DCNV2_ERR_CUDA;
     di->attr_set.fetch_or(bit, std::memory_order_acq_rel);
   }
@@ -373,6 +479,7 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
   a.scale = scale; a.precise = p.precise ? 1 : 0; a.tf32_single = p.tf32_single ? 1 : 0;
   a.timeout_ns = kDefaultTimeoutNs;
   a.use_win = 0; a.win_rows = p.win_rows; a.win_top = p.win_top; a.win_bytes = p.win_bytes;
+  a.win_stride = p.win_stride; a.a_stages = p.a_stages; a.b_stages = p.b_stages;
   CUtensorMap tmap;
   std::memset(&tmap, 0, sizeof(tmap));
   if (p.use_win) {
@@ -388,7 +495,8 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
     const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
     PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
     if (encode && encode(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, x_nhwc, dims, strides, box,
-                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         p.ta ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
       a.use_win = 1;  // otherwise every corner is read from global memory
@@ -398,6 +506,34 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
   const bool k3 = p.T == 9;
   cudaError_t e = cudaSuccess;
   if constexpr (kCanPair) {
+    if (p.ta) {
+      FusedFn kfn;
+      if constexpr (PREC == PREC_F16) {
+        if (p.precise) kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, true, 0, true>
+                                    : dcnv2_fused_ta_kernel<PREC, true, 0, false>;
+        else if (k3) kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, false, 9, true>
+                                  : dcnv2_fused_ta_kernel<PREC, false, 9, false>;
+        else kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, false, 0, true>
+                          : dcnv2_fused_ta_kernel<PREC, false, 0, false>;
+      } else {
+        kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, false, 0, true>
+                     : dcnv2_fused_ta_kernel<PREC, false, 0, false>;
+      }
+      if (p.pair) {
+        const int nc = (p.num_tiles < di->sm_count / 2) ? p.num_tiles : di->sm_count / 2;
+        cudaLaunchConfig_t cfg = pair_launch_config(2 * nc, p.smem_bytes, st);
+        cfg.blockDim = dim3(kTaThreads, 1, 1);
+        cudaLaunchAttribute at = cfg.attrs[0];
+        cfg.attrs = &at;
+        e = cudaLaunchKernelEx(&cfg, kfn, a, tmap);
+      } else {
+        const int grid = p.num_tiles < di->sm_count ? p.num_tiles : di->sm_count;
+        kfn<<<grid, kTaThreads, p.smem_bytes, st>>>(a, tmap);
+        e = cudaGetLastError();
+      }
+      mk.mark(st);
+      return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
+    }
     if (p.pair) {
       FusedFn kfn = k3 ? dcnv2_fused_kernel<PREC, false, 9, true>
                        : dcnv2_fused_kernel<PREC, false, 0, true>;

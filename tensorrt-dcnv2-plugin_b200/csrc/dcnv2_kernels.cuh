@@ -90,6 +90,8 @@ struct FusedArgs {
   int win_rows;            // rows of x in one window (all W columns, 128 bytes per pixel)
   int win_top;             // window top row = first output row of the tile * stride - win_top
   uint32_t win_bytes;      // win_rows * W * 128
+  uint32_t win_stride;     // distance of the two window buffers (win_bytes rounded up to 1 KB)
+  int a_stages, b_stages;  // A operand in TMEM: A ring (TMEM) and B ring (shared memory) depths
   int precise;             // fp16: fp32 sampler arithmetic
   int tf32_single;         // fp32: hi*hi only (plain TF32)
   unsigned long long timeout_ns;

@@ -317,3 +317,47 @@ def test_cta_pair_and_single_cta_paths_agree(shape, monkeypatch):
     # same A and B operands and K order: the two paths differ at most by fp32 accumulation order
     assert mean_rel(y16_pair, y16_one) <= 1e-4
     np.testing.assert_allclose(y8_pair, y8_one, rtol=1e-6, atol=1e-6)
+
+
+TA_SHAPES = {
+    # identity-like offsets: every corner in the x window (fp16 3x3 fast path)
+    "c256_o256_hw64_idlike": dict(n=2, c=256, o=256, h=64, w=64, ostd=0.1),
+    # out-of-image offsets: corners outside the window come from global memory
+    "c256_o256_oob": dict(n=1, c=256, o=256, h=32, w=48, ostd=0.5, outl=0.05),
+    # partial channel block (16 of 64 / 128 channels), 5x5 taps
+    "c16_o24_k5": dict(n=2, c=16, o=24, h=19, w=23, k=5, p=2),
+    "c64_o48_k1": dict(n=2, c=64, o=48, h=20, w=20, k=1, p=0),
+    # two output-channel chunks of 256, groups, dilation 2
+    "c128_o512_dg8_d2": dict(n=1, c=128, o=512, h=24, w=24, p=2, d=2, dg=8, ostd=2.0),
+    # odd pixel count (single-pixel epilogue stores), stride 2
+    "c32_o24_s2": dict(n=3, c=32, o=24, h=33, w=29, s=2),
+    # W > 256: no x window, every corner from global memory
+    "c16_o32_w300": dict(n=1, c=16, o=32, h=5, w=300),
+}
+
+
+@pytest.mark.parametrize("pair", [False, True], ids=["cta", "pair"])
+@pytest.mark.parametrize("shape", sorted(TA_SHAPES))
+def test_tmem_a_kernel_matches_smem_a_kernel(shape, pair, monkeypatch):
+    """fp16 / int8 default to the kernel with the A operand in tensor memory
+    (DCNV2_KERNEL=ta also forces it for > 256 output channels); DCNV2_KERNEL=smem selects the
+    shared-memory A kernel. Both meet the stated bounds against the oracle and agree with each
+    other (same A values, same K order)."""
+    fx = random_case(**TA_SHAPES[shape])
+    h = half_inputs(fx)
+    ref16 = oracle.forward_ref(h["x"], h["offset"], h["mask"], h["weight"], h["bias"],
+                               *oattrs(fx), precision="fp16")
+    xq, xs, wq, ws = quantized(fx)
+    if pair:
+        monkeypatch.setenv("DCNV2_PAIR", "1")
+    out = {}
+    for kern in ("smem", "ta"):
+        monkeypatch.setenv("DCNV2_KERNEL", kern)
+        out[kern] = (run_fp16(fx), run_fp16(fx, Math.PRECISE), run_int8(fx, xq, xs, wq, ws))
+    for kern, (y16, y16p, y8) in out.items():
+        assert mean_rel(y16, ref16) <= FP16_MEAN_REL, kern
+        assert mean_rel(y16p, ref16) <= FP16_MEAN_REL, kern
+        check_int8(fx, y8, xq, xs, wq, ws)
+    assert mean_rel(out["ta"][0], out["smem"][0]) <= 1e-4
+    assert mean_rel(out["ta"][1], out["smem"][1]) <= 1e-4
+    np.testing.assert_allclose(out["ta"][2], out["smem"][2], rtol=1e-6, atol=1e-6)
