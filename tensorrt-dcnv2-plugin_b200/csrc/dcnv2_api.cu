@@ -146,8 +146,8 @@ int max_tile_rows(const Plan& p, int tile_px) {
 }
 
 // Configuration of dcnv2_fused_ta_kernel: one accumulator of n_mma <= 256 columns and up to 8
-// A stages of 32 columns in 512 TMEM columns; shared memory holds two x windows (1 KB aligned,
-// 128-byte swizzle) and the B ring. The window covers, for every pixel of a CTA's 128, the taps
+// A stages of 32 columns in 512 TMEM columns; shared memory holds two x windows (1 KB aligned)
+// and the B ring. The window covers, for every pixel of a CTA's 128, the taps
 // whose offsets lie in (-1 - M, 1 + M) for the largest margin M <= 2 that still leaves three B
 // stages (else two); corners outside it are read from global memory.
 void plan_ta(Plan* pl) {
@@ -159,7 +159,7 @@ void plan_ta(Plan* pl) {
   p.nrows = p.n_mma;
   p.acc_bufs = 1;
   p.tmem_cols = kTaTmemCols;
-  p.a_stages = kTaMaxAStages;
+  p.a_stages = p.prec == PREC_F16 ? TaLayout<PREC_F16>::kAStages : TaLayout<PREC_I8>::kAStages;
   p.a_stage_bytes = 0;
   p.b_kb_bytes = size_t(p.nrows) * kRowBytes;
   p.b_stage_bytes = static_cast<uint32_t>(p.b_kb_bytes / (p.pair ? 2 : 1));
@@ -167,7 +167,7 @@ void plan_ta(Plan* pl) {
   p.tiles_per_img = static_cast<int>(p.pair ? cdiv(int64_t(p.Ho) * p.Wo, 2 * kTileM)
                                             : cta_tiles_per_img);
   p.num_tiles = static_cast<int>(int64_t(p.N) * p.tiles_per_img * p.cchunks);
-  const size_t fixed = 1024 + 512;
+  const size_t fixed = 1024 + 512 + 1024;  // alignment slack, barriers, staged bias (fp32)
   const size_t per_stage = p.b_stage_bytes;
   auto b_stages_for = [&](size_t win_total) {
     int sb = static_cast<int>((kSmemLimit - fixed - win_total) / per_stage);
@@ -495,8 +495,7 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
     const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
     PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
     if (encode && encode(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, x_nhwc, dims, strides, box,
-                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         p.ta ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
       a.use_win = 1;  // otherwise every corner is read from global memory

@@ -17,8 +17,10 @@
 //                stores of y (two pixels per store where the layout allows)
 //   warps 6-17   samplers: warp w fills TMEM lane quadrant w % 4 (32 pixels, thread = pixel),
 //                whole 128-byte rows of the K-blocks of taps t = (w - 6) / 4 (mod 3)
-// The x window is loaded with the 128-byte swizzle (chunk c of window pixel i at chunk c ^ (i % 8)),
-// so the 32 pixels of a warp that read the same logical chunk spread over all banks.
+// The x window is stored linearly (128 bytes per pixel, so 16-byte chunk c of any pixel sits in
+// bank group c). In the 3x3 fp16 fast path lane i reads chunk h ^ (i % 8) at step h: the 8 lanes
+// of each 128-bit load phase hit 8 different bank groups whatever the offsets, and a register
+// butterfly restores the chunk order before the TMEM store.
 #pragma once
 #include "dcnv2_kernels.cuh"
 
@@ -27,6 +29,15 @@ namespace dcnv2 {
 constexpr uint32_t kTaAccCols = 256;   // accumulator: one 32-bit column per output channel
 constexpr uint32_t kTaStageCols = 32;  // one A K-block: 128 bytes of every TMEM lane
 constexpr int kTaMaxAStages = 8;       // (512 - 256) / 32
+// fp16: the epilogue parks the converted tile (256 fp16 channels of each pixel = 128 columns)
+// next to the accumulator and releases the accumulator before it stores y, so the MMAs of the
+// next tile wait only for the TMEM-to-TMEM drain; 4 A stages remain.
+constexpr uint32_t kTaParkCols = 128;
+template <int PREC> struct TaLayout {
+  static constexpr bool kPark = PREC == PREC_F16;
+  static constexpr uint32_t kACol0 = kTaAccCols + (kPark ? kTaParkCols : 0);
+  static constexpr int kAStages = kPark ? 4 : kTaMaxAStages;
+};
 constexpr uint32_t kTaTmemCols = 512;
 constexpr int kTaMaxBStages = 8;
 constexpr int kTaTapGroups = 3;        // sampler warps per TMEM lane quadrant
@@ -51,7 +62,7 @@ __device__ __noinline__ void ta_mma_issuer(const TaMmaParams mp) {
   const uint32_t idesc = PREC == PREC_F16 ? ptx::make_idesc(1, 0, mp.n_mma, m)
                                           : ptx::make_idesc(2, 1, mp.n_mma, m);
   const uint64_t desc0 = ptx::sw128_kmajor_desc(0);
-  const uint32_t a_tm0 = mp.tmem_base + kTaAccCols;
+  const uint32_t a_tm0 = mp.tmem_base + TaLayout<PREC>::kACol0;
   const WaitCtx& wc = mp.wc;
   int sa = 0, sb = 0;
   uint32_t pa = 0, pb = 0, use = 0;
@@ -62,16 +73,30 @@ __device__ __noinline__ void ta_mma_issuer(const TaMmaParams mp) {
       break;
     }
     ptx::tc_fence_after();
+    // `ready`: the barriers of K-block kb were found complete by the look-ahead test made while
+    // the previous K-block's MMAs were queued (its latency overlaps tensor work)
+    bool ready = false;
     for (int kb = 0; kb < mp.numKB; ++kb) {
-      if (!wait_bar(mp.a_full + 8 * sa, pa, wc, DCNV2_DEVERR_TIMEOUT_MMA) ||
-          !wait_bar(mp.b_full + 8 * sb, pb, wc, DCNV2_DEVERR_TIMEOUT_MMA) ||
-          (PAIR && !wait_bar<0, true>(mp.peer_full + 8 * sa, pa, wc, DCNV2_DEVERR_TIMEOUT_MMA))) {
-        ok = false;
-        break;
+      if (!ready) {
+        if (!wait_bar(mp.b_full + 8 * sb, pb, wc, DCNV2_DEVERR_TIMEOUT_MMA) ||
+            !wait_bar(mp.a_full + 8 * sa, pa, wc, DCNV2_DEVERR_TIMEOUT_MMA) ||
+            (PAIR && !wait_bar<0, true>(mp.peer_full + 8 * sa, pa, wc, DCNV2_DEVERR_TIMEOUT_MMA))) {
+          ok = false;
+          break;
+        }
       }
       ptx::tc_fence_after();
       const uint32_t at = a_tm0 + static_cast<uint32_t>(sa) * kTaStageCols;
       const uint64_t bd0 = desc0 | (((mp.b_base + sb * mp.b_stage_bytes) >> 4) & 0x3FFFu);
+      // next stage indices, and a non-blocking test of its barriers
+      const int sa1 = sa + 1 == mp.SA ? 0 : sa + 1, sb1 = sb + 1 == mp.SB ? 0 : sb + 1;
+      const uint32_t pa1 = sa + 1 == mp.SA ? pa ^ 1u : pa, pb1 = sb + 1 == mp.SB ? pb ^ 1u : pb;
+      uint32_t nxt = 0;
+      if (kb + 1 < mp.numKB) {
+        nxt = ptx::mbar_test_wait(mp.b_full + 8 * sb1, pb1) &
+              ptx::mbar_test_wait(mp.a_full + 8 * sa1, pa1);
+        if (PAIR) nxt &= ptx::mbar_test_wait_cluster(mp.peer_full + 8 * sa1, pa1);
+      }
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         // K-step k: 8 TMEM columns of A, 32 bytes further along the B rows
@@ -91,8 +116,8 @@ __device__ __noinline__ void ta_mma_issuer(const TaMmaParams mp) {
         ptx::tc_commit(mp.a_empty + 8 * sa);
         ptx::tc_commit(mp.b_empty + 8 * sb);
       }
-      if (++sa == mp.SA) { sa = 0; pa ^= 1u; }
-      if (++sb == mp.SB) { sb = 0; pb ^= 1u; }
+      sa = sa1; sb = sb1; pa = pa1; pb = pb1;
+      ready = nxt != 0;
     }
     if (!ok) break;
     if (PAIR) ptx::tc_commit_pair(mp.tfull, 3);
@@ -107,9 +132,8 @@ __device__ __noinline__ void ta_mma_issuer(const TaMmaParams mp) {
 // Bilinear geometry of tap t for one pixel: the four corner weights (mask folded in, zero when a
 // corner or the sample centre is outside the image; the rules of bilinear<T>,
 // src/dcn_kernel.cu:19-30) and where each corner is read: loc >= 0 is the byte offset, inside
-// the swizzled window, of 16-byte chunk 0 of the corner pixel (chunk h is at loc ^ (16 h));
-// loc < 0 is -(pixel index in the channels-last image) - 1. Operations and their order match
-// make_geom.
+// the window of the corner pixel (chunk h is at loc + 16 h); loc < 0 is -(pixel index in the
+// channels-last image) - 1. Operations and their order match make_geom.
 __device__ __forceinline__ void ta_tap_geom(const FusedArgs& a, bool valid, int bh, int bw,
                                             float dh, float dw, float m, int row0,
                                             float (&wt)[4], int (&loc)[4]) {
@@ -131,11 +155,32 @@ __device__ __forceinline__ void ta_tap_geom(const FusedArgs& a, bool valid, int 
     wt[c] = cok ? __fmul_rn(m, __fmul_rn(fy, fx)) : 0.f;
     if (a.use_win && (!cok || (hc >= row0 && hc < row0 + a.win_rows))) {
       const int wp = cok ? (hc - row0) * a.W + wc : 0;
-      loc[c] = wp * kRowBytes + ((wp & 7) << 4);  // chunk 0 after the swizzle
+      loc[c] = wp * kRowBytes;
     } else {
       loc[c] = -(cok ? hc * a.W + wc : 0) - 1;
     }
   }
+}
+
+// Slot h of `o` (words 4h..4h+3) holds chunk h ^ r; afterwards slot c holds chunk c. Three
+// conditional exchanges of slots h and h ^ 2^b (b = 0, 1, 2), each when bit b of r is set.
+template <int B>
+__device__ __forceinline__ void xchg_slots(uint32_t (&o)[32], bool p) {
+#pragma unroll
+  for (int h = 0; h < 8; ++h) {
+    if (h & (1 << B)) continue;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t a = o[4 * h + w], b = o[4 * (h | (1 << B)) + w];
+      o[4 * h + w] = p ? b : a;
+      o[4 * (h | (1 << B)) + w] = p ? a : b;
+    }
+  }
+}
+__device__ __forceinline__ void unrotate_chunks(uint32_t (&o)[32], int r) {
+  xchg_slots<0>(o, r & 1);
+  xchg_slots<1>(o, r & 2);
+  xchg_slots<2>(o, r & 4);
 }
 
 template <int PREC, bool PRECISE, int KT, bool PAIR>
@@ -150,7 +195,7 @@ __global__ void __launch_bounds__(kTaThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int SA = args.a_stages, SB = args.b_stages;
-  // [2 windows (1 KB aligned, swizzled) | SB B stages | barriers]
+  // [2 windows (1 KB aligned) | SB B stages | barriers | bias]
   uint8_t* w_smem = smem;
   uint8_t* b_smem = smem + (args.use_win ? 2 * args.win_stride : 0);
   uint64_t* bars = reinterpret_cast<uint64_t*>(b_smem + static_cast<size_t>(SB) * args.b_stage_bytes);
@@ -166,6 +211,8 @@ __global__ void __launch_bounds__(kTaThreads, 1)
   const uint32_t win_empty = win_full + 16;       // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * SA + 2 * SB + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // bias of the (single) output-channel chunk as fp32, after the 512 bytes of barriers
+  float* bias_smem = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 512);
   const WaitCtx wc{args.timeout_ns, args.err, abort_flag};
   const int rank = PAIR ? static_cast<int>(ptx::cluster_ctarank()) : 0;
   const int tile0 = PAIR ? static_cast<int>(ptx::cluster_id_x()) : static_cast<int>(blockIdx.x);
@@ -191,6 +238,15 @@ __global__ void __launch_bounds__(kTaThreads, 1)
     }
     *abort_flag = 0;
     ptx::fence_mbar_init();
+  }
+  if (args.cchunks == 1) {
+    for (int i = threadIdx.x; i < args.n_mma; i += blockDim.x) {
+      float bv = 0.f;
+      if (args.bias && i < args.O)
+        bv = PREC == PREC_F16 ? __half2float(reinterpret_cast<const __half*>(args.bias)[i])
+                              : reinterpret_cast<const float*>(args.bias)[i];
+      bias_smem[i] = bv;
+    }
   }
   if (warp == kMmaWarp) {
     if (PAIR) {
@@ -275,16 +331,20 @@ __global__ void __launch_bounds__(kTaThreads, 1)
     }
   } else if (warp < kSampWarp0) {
     // ------------------------------------------------------------ epilogue
+    // Per 16 accumulator columns: tcgen05.ld (the next block's load overlaps this block's
+    // stores), + bias from shared memory (staged at kernel start; a global load per column
+    // would wait for L2 on every block, since the L1 left beside 225 KB of shared memory is
+    // small), convert, store. Lanes 2i and 2i+1 swap one value per channel pair so that each
+    // store covers two pixels, when every pixel pair starts on an aligned address.
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    // Two pixels per store (lanes 2i and 2i+1 swap one value per channel pair) when every
-    // pixel pair starts on an aligned address.
     const bool paired = (args.P % 2) == 0 &&
                         (reinterpret_cast<uintptr_t>(args.y) % (2 * sizeof(YT))) == 0;
+    const bool staged = args.cchunks == 1;
     const int odd = lane & 1;
     int tl = 0;
     for (int tile = tile0; tile < args.num_tiles; tile += tstep, ++tl) {
       const bool got = wait_bar<kSuspend, false>(tfull, static_cast<uint32_t>(tl) & 1u, wc,
-                                            DCNV2_DEVERR_TIMEOUT_EPILOGUE);
+                                                 DCNV2_DEVERR_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, got)) break;
       ptx::tc_fence_after();
       int img, pt, cc;
@@ -293,25 +353,31 @@ __global__ void __launch_bounds__(kTaThreads, 1)
       const int pe = p - odd;  // first pixel of this lane's pair
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
       const int o_chunk = cc * args.n_mma;
+      const int ncols = args.O - o_chunk < args.n_mma ? args.O - o_chunk : args.n_mma;
       YT* yimg = reinterpret_cast<YT*>(args.y) + static_cast<size_t>(img) * args.O * args.P;
-      for (int col = 0; col < args.n_mma; col += 16) {
+      auto block = [&](const uint32_t (&r)[16], int col) {
         const int o0 = o_chunk + col;
-        if (o0 >= args.O) break;  // warp-uniform
-        uint32_t r[16];
-        ptx::tmem_ld_32x32b_x16(taddr + col, r);
-        ptx::tmem_wait_ld();
+        float bo[16];
+        if (staged) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            const float4 b4 = *reinterpret_cast<const float4*>(bias_smem + col + i);
+            bo[i] = b4.x; bo[i + 1] = b4.y; bo[i + 2] = b4.z; bo[i + 3] = b4.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int o = o0 + i < args.O ? o0 + i : args.O - 1;
+            bo[i] = !args.bias ? 0.f
+                    : PREC == PREC_F16 ? __half2float(reinterpret_cast<const __half*>(args.bias)[o])
+                                       : __ldg(reinterpret_cast<const float*>(args.bias) + o);
+          }
+        }
         float v[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int o = o0 + i < args.O ? o0 + i : args.O - 1;
-          if (PREC == PREC_F16) {
-            const float bo =
-                args.bias ? __half2float(reinterpret_cast<const __half*>(args.bias)[o]) : 0.f;
-            v[i] = __uint_as_float(r[i]) + bo;
-          } else {
-            const float bo = args.bias ? __ldg(reinterpret_cast<const float*>(args.bias) + o) : 0.f;
-            v[i] = __fmaf_rn(__int2float_rn(static_cast<int>(r[i])), args.scale, bo);
-          }
+          if (PREC == PREC_F16) v[i] = __uint_as_float(r[i]) + bo[i];
+          else v[i] = __fmaf_rn(__int2float_rn(static_cast<int>(r[i])), args.scale, bo[i]);
         }
         if (paired) {
 #pragma unroll
@@ -325,11 +391,8 @@ __global__ void __launch_bounds__(kTaThreads, 1)
             const int o = o0 + 2 * i + odd;
             if (o < args.O && pe < args.P) {
               YT* dst = yimg + static_cast<size_t>(o) * args.P + pe;
-              if (PREC == PREC_F16) {
-                *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(lo, hi);
-              } else {
-                *reinterpret_cast<float2*>(dst) = make_float2(lo, hi);
-              }
+              if (PREC == PREC_F16) *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(lo, hi);
+              else *reinterpret_cast<float2*>(dst) = make_float2(lo, hi);
             }
           }
         } else if (p < args.P) {
@@ -343,12 +406,97 @@ __global__ void __launch_bounds__(kTaThreads, 1)
             }
           }
         }
-      }
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (PAIR && rank != 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(tempty, 0));
-        else ptx::mbar_arrive(tempty);
+      };
+      auto release = [&]() {
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (PAIR && rank != 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(tempty, 0));
+          else ptx::mbar_arrive(tempty);
+        }
+      };
+      uint32_t ra[16], rb[16];
+      if constexpr (TaLayout<PREC>::kPark) {
+        // 1) accumulator + bias -> fp16 pairs in the park columns, then release the accumulator
+        const uint32_t park = taddr + kTaAccCols;
+        auto drain = [&](uint32_t (&r)[16], int col) {
+          uint32_t h[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float2 b2 = staged ? *reinterpret_cast<const float2*>(bias_smem + col + 2 * i)
+                                     : make_float2(0.f, 0.f);
+            float b0 = b2.x, b1 = b2.y;
+            if (!staged && args.bias) {
+              const int o = o_chunk + col + 2 * i;
+              const __half* bp = reinterpret_cast<const __half*>(args.bias);
+              b0 = o < args.O ? __half2float(bp[o]) : 0.f;
+              b1 = o + 1 < args.O ? __half2float(bp[o + 1]) : 0.f;
+            }
+            h[i] = h2_bits(__floats2half2_rn(__uint_as_float(r[2 * i]) + b0,
+                                             __uint_as_float(r[2 * i + 1]) + b1));
+          }
+          ptx::tmem_st_32x32b_x8(park + col / 2, h);
+        };
+        ptx::tmem_ld_32x32b_x16(taddr, ra);
+        for (int col = 0; col < ncols; col += 32) {  // warp-uniform bounds
+          ptx::tmem_wait_ld_regs(ra);
+          if (col + 16 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 16, rb);
+          drain(ra, col);
+          if (col + 16 < ncols) {
+            ptx::tmem_wait_ld_regs(rb);
+            if (col + 32 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 32, ra);
+            drain(rb, col + 16);
+          }
+        }
+        release();
+        ptx::tmem_wait_st();
+        // 2) stores of y from the park columns, while the MMAs of the next tile run
+        auto store = [&](const uint32_t (&w)[16], int col) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int o = o_chunk + col + 2 * i;  // channels o, o + 1 in word i
+            if (paired) {
+              // lanes (2j, 2j+1): the even lane stores channel o, the odd one o + 1, both for
+              // pixels (pe, pe + 1)
+              const uint32_t recv = __shfl_xor_sync(0xffffffffu, w[i], 1);
+              const uint32_t pr = odd ? __byte_perm(recv, w[i], 0x7632)
+                                      : __byte_perm(w[i], recv, 0x5410);
+              if (o + odd < args.O && pe < args.P)
+                *reinterpret_cast<uint32_t*>(yimg + static_cast<size_t>(o + odd) * args.P + pe) = pr;
+            } else if (p < args.P) {
+              if (o < args.O)
+                *reinterpret_cast<unsigned short*>(yimg + static_cast<size_t>(o) * args.P + p) =
+                    static_cast<unsigned short>(w[i] & 0xFFFFu);
+              if (o + 1 < args.O)
+                *reinterpret_cast<unsigned short*>(yimg + static_cast<size_t>(o + 1) * args.P + p) =
+                    static_cast<unsigned short>(w[i] >> 16);
+            }
+          }
+        };
+        ptx::tmem_ld_32x32b_x16(park, ra);
+        for (int col = 0; col < ncols; col += 64) {  // 32 channels per load
+          ptx::tmem_wait_ld_regs(ra);
+          if (col + 32 < ncols) ptx::tmem_ld_32x32b_x16(park + col / 2 + 16, rb);
+          store(ra, col);
+          if (col + 32 < ncols) {
+            ptx::tmem_wait_ld_regs(rb);
+            if (col + 64 < ncols) ptx::tmem_ld_32x32b_x16(park + col / 2 + 32, ra);
+            store(rb, col + 32);
+          }
+        }
+      } else {
+        ptx::tmem_ld_32x32b_x16(taddr, ra);
+        for (int col = 0; col < ncols; col += 32) {  // warp-uniform bounds
+          ptx::tmem_wait_ld_regs(ra);
+          if (col + 16 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 16, rb);
+          block(ra, col);
+          if (col + 16 < ncols) {
+            ptx::tmem_wait_ld_regs(rb);
+            if (col + 32 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 32, ra);
+            block(rb, col + 16);
+          }
+        }
+        release();
       }
     }
   } else {
@@ -367,8 +515,10 @@ __global__ void __launch_bounds__(kTaThreads, 1)
     const int q = warp & 3;
     const int j = sw >> 2;  // tap group
     const int mrow = q * 32 + lane;
-    const uint32_t a_tm = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + kTaAccCols;
+    constexpr int SAC = TaLayout<PREC>::kAStages;  // power of two
+    const uint32_t a_tm = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + TaLayout<PREC>::kACol0;
     const bool issuer = args.use_win && sw == 0 && lane == 0;
+    const uint32_t rot16 = static_cast<uint32_t>(lane & 7) << 4;  // fast path: chunk rotation
     const GT* offp = reinterpret_cast<const GT*>(args.offset);
     const GT* maskp = reinterpret_cast<const GT*>(args.mask);
     const uint32_t w_base = ptx::smem_addr(w_smem);
@@ -439,8 +589,8 @@ __global__ void __launch_bounds__(kTaThreads, 1)
     // number) is free; returns its first TMEM column address for this warp's lanes.
     auto acquire = [&](int kb, uint32_t& ta) -> bool {
       flush();
-      const int s = kb % kTaMaxAStages;
-      const uint32_t ph = static_cast<uint32_t>(kb / kTaMaxAStages) & 1u;
+      const int s = kb & (SAC - 1);
+      const uint32_t ph = static_cast<uint32_t>(kb / SAC) & 1u;
       const bool got = wait_bar<kSuspend>(a_empty + 8 * s, ph ^ 1u, wc, DCNV2_DEVERR_TIMEOUT_SAMPLER);
       if (!__all_sync(0xffffffffu, got)) return false;
       ptx::tc_fence_after();
@@ -472,7 +622,7 @@ __global__ void __launch_bounds__(kTaThreads, 1)
         // the MMA may be waiting for this warp's last stage while the geometry loads run
         flush();
         // fp16 fast path: the 4 corners of each of this warp's taps as
-        // (fp16 weight | window byte offset of chunk 0 of the corner pixel << 16)
+        // (fp16 weight | window byte offset of the corner pixel << 16)
         uint32_t cw[kMyTaps][4];
         bool fast_g = false;
         if (kFast) {
@@ -521,31 +671,32 @@ __global__ void __launch_bounds__(kTaThreads, 1)
 #pragma unroll
               for (int c = 0; c < 4; ++c) {
                 const uint32_t v = cw[u][c];
-                pix[c] = win + (v >> 16);  // chunk 0 of the corner pixel
+                pix[c] = win + (v >> 16);  // the corner pixel's 128 bytes
                 wh[c] = __half2half2(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu)));
               }
-              // the row in two halves of 4 chunks: 16 output registers live, not 32
-              uint32_t ta = 0;
+              // step h: chunk h ^ rot of every corner (conflict-free phases), mixed into out[4h..]
+              uint32_t out[32];
 #pragma unroll
-              for (int half = 0; half < 2; ++half) {
-                uint32_t out[16];
+              for (int h = 0; h < 8; ++h) {
+                const uint32_t co = (static_cast<uint32_t>(h) << 4) ^ rot16;
+                uint4 xv[4];
 #pragma unroll
-                for (int hh = 0; hh < 4; ++hh) {
-                  const uint32_t h = static_cast<uint32_t>(4 * half + hh);
-                  uint4 xv[4];
-#pragma unroll
-                  for (int c = 0; c < 4; ++c) xv[c] = ptx::ld_shared_v4(pix[c] ^ (h << 4));
-                  out[4 * hh + 0] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].x, xv[1].x, xv[2].x, xv[3].x);
-                  out[4 * hh + 1] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].y, xv[1].y, xv[2].y, xv[3].y);
-                  out[4 * hh + 2] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].z, xv[1].z, xv[2].z, xv[3].z);
-                  out[4 * hh + 3] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].w, xv[1].w, xv[2].w, xv[3].w);
-                  // chunk h is mixed before the loads of chunk h + 1 are issued
-                  asm volatile("" : "+r"(out[4 * hh + 0]), "+r"(out[4 * hh + 1]),
-                               "+r"(out[4 * hh + 2]), "+r"(out[4 * hh + 3]));
-                }
-                if (half == 0 && !acquire(kb_seq + t, ta)) { ok = false; break; }
-                ptx::tmem_st_32x32b_x16(ta + 16 * half, out);
+                for (int c = 0; c < 4; ++c) xv[c] = ptx::ld_shared_v4(pix[c] + co);
+                // the previous K-block's TMEM store has had time to land: publish it now rather
+                // than after this whole K-block
+                if (h == 0) flush();
+                out[4 * h + 0] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].x, xv[1].x, xv[2].x, xv[3].x);
+                out[4 * h + 1] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].y, xv[1].y, xv[2].y, xv[3].y);
+                out[4 * h + 2] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].z, xv[1].z, xv[2].z, xv[3].z);
+                out[4 * h + 3] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].w, xv[1].w, xv[2].w, xv[3].w);
+                // chunk h is mixed before the loads of chunk h + 1 are issued
+                asm volatile("" : "+r"(out[4 * h + 0]), "+r"(out[4 * h + 1]),
+                             "+r"(out[4 * h + 2]), "+r"(out[4 * h + 3]));
               }
+              unrotate_chunks(out, lane & 7);
+              uint32_t ta = 0;
+              if (!acquire(kb_seq + t, ta)) { ok = false; break; }
+              ptx::tmem_st_32x32b_x32(ta, out);
               if (!ok) break;
               pending = true;
             }
