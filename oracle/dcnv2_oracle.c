@@ -15,9 +15,11 @@
  *                          [g*T, (g+1)*T) and input channels [g*C/dg, (g+1)*C/dg)
  *
  * oracle_forward_i8_exact() is the exact int32-domain INT8 definition that the tensor-core
- * kernel implements: each column value is requantised as clamp(rint(v), -127, 127) where v is
- * the mask-folded bilinear sample computed with the single-precision operation sequence written
- * out below, and the products are summed exactly in integers.
+ * kernels implement. Each column value is the bilinear sample of int8 x requantised in fixed
+ * point: the mask is clamped to [0, 1] (NaN -> 0), the corner weights a_k = m * fy * fx are
+ * formed in single precision as written below, w_k = min(rint(a_k * 65536), 65535) (0 for
+ * NaN or a_k <= 0), and c = floor((sum_k w_k * x_k + 32768) / 65536), always in [-128, 127]
+ * (|c - m * bilinear(x)| <= 0.5 + 2^-7). The products w_q * c are summed exactly in integers.
  *
  * Compile with -ffp-contract=off so that every float operation rounds as written.
  */
@@ -267,16 +269,21 @@ typedef struct {
   int8_t* cq; /* [C*T][P] */
 } qcols_ctx;
 
+static float i8_mask(float m) { return isnan(m) ? 0.f : fminf(fmaxf(m, 0.f), 1.f); }
+/* 16-bit fixed-point corner weight: rint(a * 2^16) (nearest even), 0 for NaN or a <= 0,
+ * at most 65535. */
+static int32_t i8_weight(float a) {
+  const float v = a * 65536.f; /* exact: power-of-two scaling */
+  if (!(v > 0.f)) return 0;
+  const float r = rintf(v);
+  return r >= 65535.f ? 65535 : (int32_t)r;
+}
 static int8_t requant(tap_geom* g, const int8_t* plane) {
-  float v = g->a[0] * (float)(g->idx[0] >= 0 ? plane[g->idx[0]] : 0);
-  v = fmaf(g->a[1], (float)(g->idx[1] >= 0 ? plane[g->idx[1]] : 0), v);
-  v = fmaf(g->a[2], (float)(g->idx[2] >= 0 ? plane[g->idx[2]] : 0), v);
-  v = fmaf(g->a[3], (float)(g->idx[3] >= 0 ? plane[g->idx[3]] : 0), v);
-  if (isnan(v)) return 0;
-  float r = rintf(v);
-  if (r < -127.f) r = -127.f;
-  if (r > 127.f) r = 127.f;
-  return (int8_t)r;
+  int32_t sum = 32768;
+  for (int k = 0; k < 4; ++k)
+    if (g->idx[k] >= 0) sum += i8_weight(g->a[k]) * (int32_t)plane[g->idx[k]];
+  /* floor division by 2^16 (gcc's >> on a negative int is an arithmetic shift) */
+  return (int8_t)(sum >> 16);
 }
 
 static void qcols_range(void* vctx, int64_t b, int64_t e) {
@@ -297,7 +304,7 @@ static void qcols_range(void* vctx, int64_t b, int64_t e) {
         int p = oh * q->Wo + ow;
         tap_geom gm = kernel_geom(H, W, oh * s->stride - s->padding + i * s->dilation,
                                   ow * s->stride - s->padding + j * s->dilation, dhp[p], dwp[p],
-                                  mp[p]);
+                                  i8_mask(mp[p]));
         out[p] = requant(&gm, plane);
       }
   }
@@ -323,7 +330,7 @@ static void igemm_range(void* vctx, int64_t b, int64_t e) {
 }
 
 /*
- * Exact INT8: cq = clamp(rint(v)) per column value (order of kernel_geom/requant above),
+ * Exact INT8: cq per column value by the fixed-point rule of requant() above,
  * acc = sum w_q*cq in int64, y = acc*s + b in double with s = fl32(x_scale*w_scale).
  * acc_out (optional, int64 [N][O][P]) and cols_out (optional, int8 [N][C*T][P]) expose the
  * integer intermediates so that tests can compare them bit for bit.

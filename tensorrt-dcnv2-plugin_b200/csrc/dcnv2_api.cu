@@ -422,7 +422,9 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
            set_smem_attr(dcnv2_fused_ta_kernel<PREC, true, 0, true>);
     if constexpr (PREC == PREC_I8)
       ok = ok && set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, false>) &&
-           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, true>);
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, true>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 9, false>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 9, true>);
     if (!ok) return DCNV2_ERR_CUDA;
     di->attr_set.fetch_or(bit, std::memory_order_acq_rel);
   }
@@ -514,6 +516,9 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
                                   : dcnv2_fused_ta_kernel<PREC, false, 9, false>;
         else kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, false, 0, true>
                           : dcnv2_fused_ta_kernel<PREC, false, 0, false>;
+      } else if (k3) {
+        kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, false, 9, true>
+                     : dcnv2_fused_ta_kernel<PREC, false, 9, false>;
       } else {
         kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, false, 0, true>
                      : dcnv2_fused_ta_kernel<PREC, false, 0, false>;

@@ -245,28 +245,55 @@ __device__ __forceinline__ uint32_t f16_mix_precise(const float (&a)[4], uint32_
   lo = __fmaf_rn(a[3], f3.x, lo); hi = __fmaf_rn(a[3], f3.y, hi);
   return h2_bits(__floats2half2_rn(lo, hi));
 }
-// int8: v = a0*x0 (+ a1*x1 + a2*x2 + a3*x3 by fma), c = clamp(rint(v), -127, 127).
+// ---- int8 column requantisation (fixed point, exact in integers) ----
+// A DCNv2 int8 column value is the bilinear sample of int8 x rounded to an integer:
+//   m' = clamp(m, 0, 1)        (mask; NaN -> 0), corner weights a_k = m' * fy_k * fx_k (fp32)
+//   w_k = min(rint(a_k * 2^16), 65535)                                          (u16)
+//   c   = floor((sum_k w_k * x_k + 2^15) / 2^16)                 (in [-128, 127] always)
+// |c - m' * bilinear(x)| <= 0.5 + 2^-7. dp2a forms the 2-term products and sums exactly; the
+// column byte is byte 2 of the 32-bit sum, so nothing is converted to or from floating point.
+__device__ __forceinline__ float i8_mask(float m) { return fminf(fmaxf(m, 0.f), 1.f); }
+__device__ __forceinline__ uint32_t i8_weight(float a) {
+  const uint32_t w = __float2uint_rn(__fmul_rn(a, 65536.f));  // NaN, a <= 0 -> 0
+  return w < 65535u ? w : 65535u;
+}
+// Packed weight pairs (w0 | w1 << 16) and (w2 | w3 << 16).
+__device__ __forceinline__ void i8_weight_pairs(const float (&a)[4], uint32_t& w01, uint32_t& w23) {
+  w01 = i8_weight(a[0]) | (i8_weight(a[1]) << 16);
+  w23 = i8_weight(a[2]) | (i8_weight(a[3]) << 16);
+}
+__device__ __forceinline__ int dp2a_lo_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp2a.lo.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp2a_hi_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp2a.hi.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// One word of 4 int8 channels from the same word of the 4 corners.
+__device__ __forceinline__ uint32_t i8_mix_fx(uint32_t w01, uint32_t w23, uint32_t x0, uint32_t x1,
+                                              uint32_t x2, uint32_t x3) {
+  // corner bytes paired per channel: [x0.b0 x1.b0 x0.b1 x1.b1] and [x0.b2 x1.b2 x0.b3 x1.b3]
+  const uint32_t t01l = __byte_perm(x0, x1, 0x5140), t01h = __byte_perm(x0, x1, 0x7362);
+  const uint32_t t23l = __byte_perm(x2, x3, 0x5140), t23h = __byte_perm(x2, x3, 0x7362);
+  const int s0 = dp2a_lo_us(w23, t23l, dp2a_lo_us(w01, t01l, 32768));
+  const int s1 = dp2a_hi_us(w23, t23l, dp2a_hi_us(w01, t01l, 32768));
+  const int s2 = dp2a_lo_us(w23, t23h, dp2a_lo_us(w01, t01h, 32768));
+  const int s3 = dp2a_hi_us(w23, t23h, dp2a_hi_us(w01, t01h, 32768));
+  const uint32_t p01 = __byte_perm(static_cast<uint32_t>(s0), static_cast<uint32_t>(s1), 0x0062);
+  const uint32_t p23 = __byte_perm(static_cast<uint32_t>(s2), static_cast<uint32_t>(s3), 0x0062);
+  return __byte_perm(p01, p23, 0x5410);
+}
+// Same from the fp32 corner weights (mask already clamped).
 __device__ __forceinline__ uint32_t i8_mix_word(const float (&a)[4], uint32_t x0, uint32_t x1,
                                                 uint32_t x2, uint32_t x3) {
-  uint32_t out = 0;
-#pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    const int sh = 8 * b;
-    const float v0 = static_cast<float>(static_cast<int8_t>(x0 >> sh));
-    const float v1 = static_cast<float>(static_cast<int8_t>(x1 >> sh));
-    const float v2 = static_cast<float>(static_cast<int8_t>(x2 >> sh));
-    const float v3 = static_cast<float>(static_cast<int8_t>(x3 >> sh));
-    float v = __fmul_rn(a[0], v0);
-    v = __fmaf_rn(a[1], v1, v);
-    v = __fmaf_rn(a[2], v2, v);
-    v = __fmaf_rn(a[3], v3, v);
-    int q = __float2int_rn(v);
-    q = min(max(q, -127), 127);
-    out |= (static_cast<uint32_t>(q) & 0xFFu) << sh;
-  }
-  return out;
+  uint32_t w01, w23;
+  i8_weight_pairs(a, w01, w23);
+  return i8_mix_fx(w01, w23, x0, x1, x2, x3);
 }
-// fp32: same mixing order as int8, then the 3xTF32 split hi = tf32(v), lo = tf32(v - hi).
+// fp32: v = a0*x0 (+ a1*x1 + a2*x2 + a3*x3 by fma), then the 3xTF32 split hi = tf32(v), lo = tf32(v - hi).
 __device__ __forceinline__ void f32_mix(const float (&a)[4], const uint4& x0, const uint4& x1,
                                         const uint4& x2, const uint4& x3, uint4& hi, uint4& lo) {
   const uint32_t* p0 = &x0.x; const uint32_t* p1 = &x1.x;
@@ -701,6 +728,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       // this lane's item of tap t from the pixel's (dh, dw, m)
       auto item_from = [&](int t, float dh, float dw, float m, uint32_t& wword, int& gpix) {
+        if (PREC == PREC_I8) m = i8_mask(m);
         const int ki = t / args.K, kj = t - ki * args.K;
         const float hf = __fadd_rn(static_cast<float>(my_bh + ki * args.dil), dh);
         const float wf = __fadd_rn(static_cast<float>(my_bw + kj * args.dil), dw);
@@ -1271,7 +1299,8 @@ __global__ void __launch_bounds__(256) pack_weights_plain_kernel(const float* __
 // ------------------------------------------------------------------ CUDA-core fallback
 // One thread per output element, any shape (the reference's naive kernel structure,
 // src/dcn_kernel.cu:33-65, extended to N, groups and the int8 requantisation). Column values use
-// the same geometry and mixing order as the fused kernels; fp16 columns are rounded to fp16.
+// the same geometry and mixing order as the fused kernels; fp16 columns are rounded to fp16, int8
+// columns follow the fixed-point rule at i8_mix_fx.
 struct SimtArgs {
   const void* x; const void* offset; const void* mask; const void* w; const void* bias; void* y;
   int N, C, H, W, O, Ho, Wo, P, K, T, stride, pad, dil, dg, Cg;
@@ -1302,7 +1331,8 @@ __global__ void __launch_bounds__(256) dcnv2_simt_kernel(const SimtArgs a) {
         const size_t gmsk = (static_cast<size_t>(n) * a.dg + g) * a.T + t;
         const float dh = load_geom_value(offp + goff * a.P + p);
         const float dw = load_geom_value(offp + (goff + 1) * a.P + p);
-        const float m = load_geom_value(maskp + gmsk * a.P + p);
+        float m = load_geom_value(maskp + gmsk * a.P + p);
+        if (PREC == PREC_I8) m = i8_mask(m);
         const float hf = __fadd_rn(static_cast<float>(oh * a.stride - a.pad + ki * a.dil), dh);
         const float wf = __fadd_rn(static_cast<float>(ow * a.stride - a.pad + kj * a.dil), dw);
         const bool inside = !(hf <= -1.f || hf >= static_cast<float>(a.H) || wf <= -1.f ||
@@ -1339,8 +1369,11 @@ __global__ void __launch_bounds__(256) dcnv2_simt_kernel(const SimtArgs a) {
           v = __fmaf_rn(wt[3], xv[3], v);
           const size_t widx = (static_cast<size_t>(o) * a.C + c) * a.T + t;
           if (PREC == PREC_I8) {
-            int q = __float2int_rn(v);
-            q = min(max(q, -127), 127);
+            int sum = 32768;  // fixed-point column value (rule at i8_mix_fx)
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              sum += static_cast<int>(i8_weight(wt[k])) * static_cast<int>(xv[k]);
+            const int q = sum >> 16;
             iacc += static_cast<long long>(q) * reinterpret_cast<const int8_t*>(a.w)[widx];
           } else if (PREC == PREC_F16) {
             const float cv = __half2float(__float2half_rn(v));

@@ -508,7 +508,7 @@ __global__ void __launch_bounds__(kTaThreads, 1)
     // chunk (32 x 16 bytes), mixes them and stores its row with one tcgen05.st; the store of a
     // K-block is published after the next K-block's loads and mix (one store in flight per warp).
     constexpr int EPC = TR::kChunkElems, KC = TR::kBlockElems, EB = TR::kElemBytes;
-    constexpr bool kFast = (PREC == PREC_F16 && !PRECISE && KT > 0);
+    constexpr bool kFast = (!PRECISE && KT > 0);
     constexpr int kMyTaps = kFast ? (KT + kTaTapGroups - 1) / kTaTapGroups : 1;
     constexpr uint32_t kNoWin = 0xFFFFu;
     const int sw = warp - kSampWarp0;
@@ -621,8 +621,8 @@ __global__ void __launch_bounds__(kTaThreads, 1)
       for (int g = 0; g < args.dg && ok; ++g) {
         // the MMA may be waiting for this warp's last stage while the geometry loads run
         flush();
-        // fp16 fast path: the 4 corners of each of this warp's taps as
-        // (fp16 weight | window byte offset of the corner pixel << 16)
+        // fast path (3x3): the 4 corners of each of this warp's taps as
+        // (16-bit weight | window byte offset of the corner pixel << 16)
         uint32_t cw[kMyTaps][4];
         bool fast_g = false;
         if (kFast) {
@@ -632,6 +632,7 @@ __global__ void __launch_bounds__(kTaThreads, 1)
             const int t = j + kTaTapGroups * u;
 #pragma unroll
             for (int i = 0; i < 3; ++i) gv[3 * u + i] = (my_val && t < T) ? geom(g, t, i) : 0.f;
+            if (PREC == PREC_I8) gv[3 * u + 2] = i8_mask(gv[3 * u + 2]);
           }
           bool inwin = true;
 #pragma unroll
@@ -645,7 +646,10 @@ __global__ void __launch_bounds__(kTaThreads, 1)
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               inwin = inwin && (t >= T || loc[c] >= 0);
-              const uint32_t hb = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(wt[c])));
+              // fp16: the weight's fp16 bits; int8: its 16-bit fixed-point value
+              const uint32_t hb =
+                  PREC == PREC_F16 ? static_cast<uint32_t>(__half_as_ushort(__float2half_rn(wt[c])))
+                                   : i8_weight(wt[c]);
               cw[u][c] = hb | ((loc[c] >= 0 ? static_cast<uint32_t>(loc[c]) : kNoWin) << 16);
             }
           }
@@ -674,6 +678,9 @@ __global__ void __launch_bounds__(kTaThreads, 1)
                 pix[c] = win + (v >> 16);  // the corner pixel's 128 bytes
                 wh[c] = __half2half2(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu)));
               }
+              // int8: weight pairs (w0 | w1 << 16), (w2 | w3 << 16) for dp2a
+              const uint32_t w01 = __byte_perm(cw[u][0], cw[u][1], 0x5410);
+              const uint32_t w23 = __byte_perm(cw[u][2], cw[u][3], 0x5410);
               // step h: chunk h ^ rot of every corner (conflict-free phases), mixed into out[4h..]
               uint32_t out[32];
 #pragma unroll
@@ -685,10 +692,17 @@ __global__ void __launch_bounds__(kTaThreads, 1)
                 // the previous K-block's TMEM store has had time to land: publish it now rather
                 // than after this whole K-block
                 if (h == 0) flush();
-                out[4 * h + 0] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].x, xv[1].x, xv[2].x, xv[3].x);
-                out[4 * h + 1] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].y, xv[1].y, xv[2].y, xv[3].y);
-                out[4 * h + 2] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].z, xv[1].z, xv[2].z, xv[3].z);
-                out[4 * h + 3] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].w, xv[1].w, xv[2].w, xv[3].w);
+                if (PREC == PREC_F16) {
+                  out[4 * h + 0] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].x, xv[1].x, xv[2].x, xv[3].x);
+                  out[4 * h + 1] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].y, xv[1].y, xv[2].y, xv[3].y);
+                  out[4 * h + 2] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].z, xv[1].z, xv[2].z, xv[3].z);
+                  out[4 * h + 3] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].w, xv[1].w, xv[2].w, xv[3].w);
+                } else {
+                  out[4 * h + 0] = i8_mix_fx(w01, w23, xv[0].x, xv[1].x, xv[2].x, xv[3].x);
+                  out[4 * h + 1] = i8_mix_fx(w01, w23, xv[0].y, xv[1].y, xv[2].y, xv[3].y);
+                  out[4 * h + 2] = i8_mix_fx(w01, w23, xv[0].z, xv[1].z, xv[2].z, xv[3].z);
+                  out[4 * h + 3] = i8_mix_fx(w01, w23, xv[0].w, xv[1].w, xv[2].w, xv[3].w);
+                }
                 // chunk h is mixed before the loads of chunk h + 1 are issued
                 asm volatile("" : "+r"(out[4 * h + 0]), "+r"(out[4 * h + 1]),
                              "+r"(out[4 * h + 2]), "+r"(out[4 * h + 3]));
@@ -710,6 +724,7 @@ __global__ void __launch_bounds__(kTaThreads, 1)
                 dh = geom(g, t, 0);
                 dw = geom(g, t, 1);
                 m = geom(g, t, 2);
+                if (PREC == PREC_I8) m = i8_mask(m);
               }
               float wt[4];
               int loc[4];

@@ -98,15 +98,71 @@ def test_int8_exact_definition(golden_dir):
     wmat = wq.reshape(wq.shape[0], -1).astype(np.int64)
     assert np.array_equal(acc[0].reshape(wq.shape[0], -1), wmat @ cols[0].astype(np.int64))
     # deviation from the reference INT8 path (fp32 columns) is bounded by the column rounding:
-    # |y_exact - y_ref| <= 0.5 * xs * ws * sum|w_q| (+ fp32 slack)
+    # |y_exact - y_ref| <= (0.5 + 2^-7) * xs * ws * sum|w_q| (+ fp32 slack)
     yref = oracle.forward_i8_ref(xq, fx["offset"], fx["mask"], wq, fx["bias"], xs, ws)
-    bound = 0.5 * xs * ws * np.abs(wq).reshape(wq.shape[0], -1).sum(1)
+    bound = I8_COL_DEV * xs * ws * np.abs(wq).reshape(wq.shape[0], -1).sum(1)
     dev = np.abs(y - yref).max(axis=(0, 2, 3))
     assert np.all(dev <= bound * 1.0001 + 1e-5)
     # and the INT8 result stays within the reference INT8 tolerance of the fp32 answer
     # (mean relative error < 10%, src/test_dcn_int8_gemm.cu:89)
     rel = np.abs(y - fx["y"]).sum() / np.abs(fx["y"]).sum()
     assert rel < 0.05
+
+
+I8_COL_DEV = 0.5 + 2.0 ** -7  # |c - m*bilinear(x)| of the fixed-point int8 column rule
+
+
+def i8_cols_numpy(xq, off, mask, stride=1, padding=1, dilation=1, k=3):
+    """Independent numpy statement of the int8 column rule (one image, one group):
+    m' = clip(m, 0, 1), a_k = m' * (fy * fx) in float32, w_k = min(rint(a_k * 2^16), 65535),
+    c = floor((sum_k w_k x_k + 2^15) / 2^16). Returns int cols [C*k*k, Ho*Wo]."""
+    C, H, W = xq.shape
+    Ho = (H + 2 * padding - dilation * (k - 1) - 1) // stride + 1
+    Wo = (W + 2 * padding - dilation * (k - 1) - 1) // stride + 1
+    f32 = np.float32
+    oh, ow = np.meshgrid(np.arange(Ho), np.arange(Wo), indexing="ij")
+    cols = np.zeros((C, k * k, Ho * Wo), np.int64)
+    for t in range(k * k):
+        i, j = divmod(t, k)
+        dh = off[2 * t].astype(f32)
+        dw = off[2 * t + 1].astype(f32)
+        m = np.nan_to_num(mask[t].astype(f32), nan=0.0).clip(0, 1).astype(f32)
+        hf = (oh * stride - padding + i * dilation).astype(f32) + dh
+        wf = (ow * stride - padding + j * dilation).astype(f32) + dw
+        inside = ~((hf <= -1) | (hf >= H) | (wf <= -1) | (wf >= W))
+        h0f, w0f = np.floor(hf), np.floor(wf)
+        lh, lw = (hf - h0f).astype(f32), (wf - w0f).astype(f32)
+        hh, hw = (f32(1) - lh).astype(f32), (f32(1) - lw).astype(f32)
+        h0, w0 = h0f.astype(np.int64), w0f.astype(np.int64)
+        s = np.full((C, Ho, Wo), 32768, np.int64)
+        for dy, dx, fy, fx in ((0, 0, hh, hw), (0, 1, hh, lw), (1, 0, lh, hw), (1, 1, lh, lw)):
+            hc, wc = h0 + dy, w0 + dx
+            ok = inside & (hc >= 0) & (hc <= H - 1) & (wc >= 0) & (wc <= W - 1)
+            a = (m * (fy * fx).astype(f32)).astype(f32)
+            w = np.minimum(np.rint(a.astype(np.float64) * 65536.0), 65535).astype(np.int64)
+            w = np.where(ok & (a > 0), w, 0)
+            xv = xq[:, np.clip(hc, 0, H - 1), np.clip(wc, 0, W - 1)].astype(np.int64)
+            s += w[None] * np.where(ok[None], xv, 0)
+        cols[:, t] = np.floor_divide(s, 65536).reshape(C, -1)
+    return cols.reshape(C * k * k, -1)
+
+
+def test_int8_column_rule_matches_numpy_statement(golden_dir):
+    fx = load(golden_dir, "tv_oob.npz")  # out-of-image offsets exercise the zero corners
+    xq, xs = oracle.quantize_sym(fx["x"])
+    wq, ws = oracle.quantize_sym(fx["weight"])
+    mask = fx["mask"].copy()
+    mask.reshape(-1)[::7] = 1.0   # weight 65536 -> 65535
+    mask.reshape(-1)[3::11] = 1.7  # clipped to 1
+    mask.reshape(-1)[5::13] = -0.3  # clipped to 0
+    _, _, cols = oracle.forward_i8_exact(xq, fx["offset"], mask, wq, fx["bias"], xs, ws,
+                                         fx["stride"], fx["padding"], fx["dilation"],
+                                         fx["groups"], want_cols=True)
+    assert int(fx["groups"]) == 1
+    for n in range(xq.shape[0]):
+        ref = i8_cols_numpy(xq[n], fx["offset"][n], mask[n], fx["stride"], fx["padding"],
+                            fx["dilation"], k=int(np.sqrt(fx["offset"].shape[1] // 2)))
+        assert np.array_equal(cols[n].astype(np.int64), ref)
 
 
 def test_int8_reference_path_tolerance(golden_dir):
