@@ -12,8 +12,9 @@ exceed the 126 MB L2, so no flush is needed between steps.
 
 Extra keys: roofline (dominant kernel, live CUDA-event timing of each launch), cpu_baseline
 (the oracle's CPU restatement on a bounded sample, rank 0 at N=1), e2e (host buffers through the
-plugin enqueue, copies inside the timed region), clocks (nvidia-smi sampled during the timed
-region), gpu_launches, secondary (int8 layer of the same shape).
+C ABI's host-buffer forward dcnv2_forward_host: every input uploaded and y downloaded inside the
+timed region, in image chunks overlapped with the compute), clocks (nvidia-smi sampled during the
+timed region), gpu_launches, secondary (int8 layer of the same shape).
 
 --impl reference times the reference's own CPU implementation of the path (the oracle port of
 src/dcn_kernel.cu + the reference GEMM, all host threads) on the same workload, each step a
@@ -238,39 +239,38 @@ def kernel_breakdown(inp, ws, out, stream, steps):
 
 
 def e2e_measure(inp_host, device, stream, steps, dist):
-    """Host buffers -> device (pinned, async) -> plugin enqueue -> y back to host, per step."""
-    from dcnv2_b200 import DCNv2Creator, tensor_desc
+    """Host buffers in, host buffer out, through the C ABI's host-buffer forward
+    (dcnv2_forward_host): per step the weight and bias are copied to the device and x, offset and
+    mask are uploaded, computed and y downloaded in chunks of images with the copies overlapped.
+    Every byte of every input crosses to the device and y comes back inside the timed region."""
     from dcnv2_b200 import capi
+    from dcnv2_b200.plugin import _dtype_of
     L = inp_host.layer
-    dt = {"fp32": capi.DType.FLOAT, "fp16": capi.DType.HALF, "int8": capi.DType.INT8}[inp_host.precision]
-    gdt = capi.DType.HALF if dt == capi.DType.HALF else capi.DType.FLOAT
-    plug = DCNv2Creator().create_plugin("DCNv2", {
-        "stride": L.stride, "padding": L.padding, "dilation": L.dilation, "kernel": L.kernel,
-        "deformable_groups": L.groups}).attach_to_context()
-    host = [t.contiguous().pin_memory() for t in inp_host.tensors()]
-    dev = [torch.empty_like(t, device=device) for t in host]
-    (oshape,) = plug.get_output_shapes(host[0].shape, host[3].shape)
+    host = [t.contiguous().pin_memory() for t in inp_host.tensors()]  # x, offset, mask, w, b
+    dt = _dtype_of(host[0])
+    desc = capi.make_desc(L.n, L.c, L.h, L.w, L.out_c, L.kernel, L.stride, L.padding,
+                          L.dilation, L.groups, dt)
+    oshape = capi.output_shape(desc)
     ydt = torch.float16 if dt == capi.DType.HALF else torch.float32
-    y = torch.empty(oshape, dtype=ydt, device=device)
     y_host = torch.empty(oshape, dtype=ydt).pin_memory()
-    ind = [tensor_desc(host[0].shape, dt, scale=inp_host.x_scale),
-           tensor_desc(host[1].shape, gdt), tensor_desc(host[2].shape, gdt),
-           tensor_desc(host[3].shape, dt, scale=inp_host.w_scale), tensor_desc(host[4].shape, gdt)]
-    outd = [tensor_desc(oshape, plug.get_output_data_types([dt])[0])]
-    wsz = plug.get_workspace_size(ind, outd)
+    w_dev = torch.empty_like(host[3], device=device)
+    b_dev = torch.empty_like(host[4], device=device)
+    wsz = capi.forward_host_workspace_size(desc, 0)
     ws = torch.empty(wsz, dtype=torch.uint8, device=device)
+    xs, wscale = inp_host.x_scale, inp_host.w_scale
     h2d = sum(t.numel() * t.element_size() for t in host)
     d2h = y_host.numel() * y_host.element_size()
 
     def step():
         with torch.cuda.stream(stream):
-            for d, h in zip(dev, host):
-                d.copy_(h, non_blocking=True)
-            rc = plug.enqueue(ind, outd, [d.data_ptr() for d in dev], [y.data_ptr()],
-                              ws.data_ptr(), wsz, stream.cuda_stream)
+            w_dev.copy_(host[3], non_blocking=True)
+            b_dev.copy_(host[4], non_blocking=True)
+            rc = capi.forward_host_raw(desc, host[0].data_ptr(), host[1].data_ptr(),
+                                       host[2].data_ptr(), w_dev.data_ptr(), b_dev.data_ptr(),
+                                       y_host.data_ptr(), ws.data_ptr(), wsz, xs, wscale, 0,
+                                       stream.cuda_stream)
             if rc != 0:
-                raise RuntimeError(f"enqueue failed {rc}")
-            y_host.copy_(y, non_blocking=True)
+                raise RuntimeError(f"dcnv2_forward_host failed {rc}")
 
     for _ in range(2):
         step()

@@ -6,7 +6,8 @@
  * src/dcn_plugin.cpp); the citation is given beside each declaration. Signatures use plain C
  * types and raw device pointers only, so any FFI (ctypes, cgo, JNI, a TensorRT IPluginV3 shim)
  * can bind them. All functions are thread-safe and reentrant; the library holds no global
- * handles apart from per-device launch attributes that are set once.
+ * handles apart from per-device launch attributes and, for dcnv2_forward_host, two copy streams
+ * per device, each set up once.
  *
  * Tensor contract (src/dcn_plugin.cpp:76,134; python/01_oracle_and_export.py:73-75):
  *   input 0  x       [N, C, H, W]                 linear NCHW
@@ -101,6 +102,30 @@ DCNV2_API dcnv2_status dcnv2_forward(const dcnv2_desc* desc,
                            const void* weight, const void* bias, void* y,
                            void* workspace, size_t workspace_bytes,
                            float x_scale, float w_scale, dcnv2_stream_t stream);
+
+/* ---- Host-buffer forward (copies overlapped with compute) ---- */
+
+/* Workspace bytes for dcnv2_forward_host with chunks of `images_per_chunk` images (0 picks the
+ * chunk: about an eighth of the batch). Returns 0 on a bad desc. */
+DCNV2_API size_t dcnv2_forward_host_workspace_size(const dcnv2_desc* desc,
+                                                   int32_t images_per_chunk);
+
+/* dcnv2_forward with x, offset, mask and y in HOST memory (weight and bias stay device pointers,
+ * as the plugin's constants are). The batch runs in chunks of images: the upload of chunk i+1,
+ * the forward of chunk i and the download of chunk i-1 overlap on two library-owned copy streams
+ * (created once per device) and `stream`, ordered by events. Asynchronous like cudaMemcpyAsync:
+ * y is complete when `stream` has completed. Host buffers must be page-locked for the copies to
+ * overlap (pageable memory works, serialised). Results are bit-identical to dcnv2_forward.
+ * No counterpart in the reference plugin, whose enqueue only sees device buffers
+ * (src/dcn_plugin.cpp:122-176); it serves callers that hold their tensors on the host, as the
+ * reference's latency benchmark does (TrtRunner.infer with host feeds, H2D and D2H inside the
+ * timed call: python/03_benchmark.py:102-113). */
+DCNV2_API dcnv2_status dcnv2_forward_host(const dcnv2_desc* desc, const void* x_host,
+                                          const void* offset_host, const void* mask_host,
+                                          const void* weight, const void* bias, void* y_host,
+                                          void* workspace, size_t workspace_bytes,
+                                          float x_scale, float w_scale, int32_t images_per_chunk,
+                                          dcnv2_stream_t stream);
 
 /* Size of the library's built-in static scratch buffer used by dcnv2_forward_static_scratch. */
 #define DCNV2_STATIC_SCRATCH_BYTES (32u * 1024u * 1024u)

@@ -822,6 +822,155 @@ dcnv2_status dcnv2_diag_timeout_selftest(uint32_t timeout_us, int32_t* device_co
 }  // extern "C"
 
 // ---------------------------------------------------------------------------------------------
+// Host-buffer forward: the batch in chunks of images, uploads / forwards / downloads overlapped.
+namespace {
+
+struct CopyStreams {
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  bool ok = false;
+};
+CopyStreams g_copy_streams[dcnv2::kMaxDevices];
+std::once_flag g_copy_once[dcnv2::kMaxDevices];
+
+// Two non-blocking copy streams per device, created once with that device current and kept for
+// the life of the process (like the per-device launch attributes).
+CopyStreams* copy_streams(int dev) {
+  if (dev < 0 || dev >= dcnv2::kMaxDevices) return nullptr;
+  std::call_once(g_copy_once[dev], [dev]() {
+    CopyStreams& c = g_copy_streams[dev];
+    c.ok = cudaStreamCreateWithFlags(&c.h2d, cudaStreamNonBlocking) == cudaSuccess &&
+           cudaStreamCreateWithFlags(&c.d2h, cudaStreamNonBlocking) == cudaSuccess;
+    if (!c.ok) cudaGetLastError();
+  });
+  return g_copy_streams[dev].ok ? &g_copy_streams[dev] : nullptr;
+}
+
+struct HostChunking {
+  int chunk = 0;                        // images per chunk
+  size_t x_img = 0, off_img = 0, mask_img = 0, y_img = 0;  // bytes per image
+  size_t x_off = 0, off_off = 0, mask_off = 0, y_off = 0;  // slot offsets inside a slot block
+  size_t slot_bytes = 0;                // one slot: x, offset, mask and y of a chunk
+  size_t fwd_off = 0, fwd_bytes = 0;    // dcnv2_forward workspace of a full chunk
+  size_t total = 0;
+};
+
+dcnv2_status host_chunking(const dcnv2_desc* desc, int32_t ipc, HostChunking* hc) {
+  dcnv2::Plan full;
+  const dcnv2_status s = dcnv2::make_plan(desc, &full);
+  if (s != DCNV2_OK) return s;
+  if (ipc < 0) return DCNV2_ERR_INVALID_ARG;
+  int chunk = ipc > 0 ? ipc : (full.N + 7) / 8;
+  if (chunk > full.N) chunk = full.N;
+  if (chunk < 1) chunk = 1;
+  dcnv2_desc d = *desc;
+  d.n = chunk;
+  dcnv2::Plan p;
+  if (dcnv2::make_plan(&d, &p) != DCNV2_OK) return DCNV2_ERR_INVALID_ARG;
+  const size_t eb = static_cast<size_t>(p.elem_bytes);
+  const size_t gb = p.prec == dcnv2::PREC_F16 ? 2 : 4;  // offset / mask / y elements
+  hc->chunk = chunk;
+  hc->x_img = size_t(p.C) * p.H * p.W * eb;
+  hc->off_img = size_t(2) * p.dg * p.T * p.P * gb;
+  hc->mask_img = size_t(p.dg) * p.T * p.P * gb;
+  hc->y_img = size_t(p.O) * p.P * gb;
+  size_t off = 0;
+  hc->x_off = off;    off = dcnv2::align_up(off + chunk * hc->x_img, 256);
+  hc->off_off = off;  off = dcnv2::align_up(off + chunk * hc->off_img, 256);
+  hc->mask_off = off; off = dcnv2::align_up(off + chunk * hc->mask_img, 256);
+  hc->y_off = off;    off = dcnv2::align_up(off + chunk * hc->y_img, 256);
+  hc->slot_bytes = off;
+  hc->fwd_off = 2 * off;
+  hc->fwd_bytes = p.ws_bytes;
+  hc->total = hc->fwd_off + p.ws_bytes + 256;
+  return DCNV2_OK;
+}
+
+}  // namespace
+
+extern "C" size_t dcnv2_forward_host_workspace_size(const dcnv2_desc* desc,
+                                                    int32_t images_per_chunk) {
+  HostChunking hc;
+  return host_chunking(desc, images_per_chunk, &hc) == DCNV2_OK ? hc.total : 0;
+}
+
+extern "C" dcnv2_status dcnv2_forward_host(const dcnv2_desc* desc, const void* x_host,
+                                           const void* offset_host, const void* mask_host,
+                                           const void* weight, const void* bias, void* y_host,
+                                           void* workspace, size_t workspace_bytes,
+                                           float x_scale, float w_scale,
+                                           int32_t images_per_chunk, dcnv2_stream_t stream) {
+  HostChunking hc;
+  dcnv2_status s = host_chunking(desc, images_per_chunk, &hc);
+  if (s != DCNV2_OK) return s;
+  if (!x_host || !offset_host || !mask_host || !weight || !y_host) return DCNV2_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < hc.total) return DCNV2_ERR_WORKSPACE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return DCNV2_ERR_NO_DEVICE; }
+  CopyStreams* cs = copy_streams(dev);
+  if (!cs) return DCNV2_ERR_CUDA;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(
+      dcnv2::align_up(reinterpret_cast<uintptr_t>(workspace), 256));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // events: entry, and per slot: inputs landed, forward done, output landed
+  cudaEvent_t ev[7] = {};
+  for (auto& e : ev)
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+      for (auto& f : ev) if (f) cudaEventDestroy(f);
+      cudaGetLastError();
+      return DCNV2_ERR_CUDA;
+    }
+  cudaEvent_t ev_entry = ev[0], *ev_in = ev + 1, *ev_fwd = ev + 3, *ev_out = ev + 5;
+  const int N = desc->n;
+  const uint8_t* xh = static_cast<const uint8_t*>(x_host);
+  const uint8_t* oh = static_cast<const uint8_t*>(offset_host);
+  const uint8_t* mh = static_cast<const uint8_t*>(mask_host);
+  uint8_t* yh = static_cast<uint8_t*>(y_host);
+  bool ok = cudaEventRecord(ev_entry, st) == cudaSuccess &&  // earlier work on `stream` first
+            cudaStreamWaitEvent(cs->h2d, ev_entry, 0) == cudaSuccess &&
+            cudaStreamWaitEvent(cs->d2h, ev_entry, 0) == cudaSuccess;
+  int i = 0;
+  for (int n0 = 0; ok && n0 < N; n0 += hc.chunk, ++i) {
+    const int nb = N - n0 < hc.chunk ? N - n0 : hc.chunk;
+    const int b = i & 1;
+    uint8_t* slot = ws + b * hc.slot_bytes;
+    // upload (slot b is free once the forward of chunk i-2 has read it)
+    if (i >= 2) ok = ok && cudaStreamWaitEvent(cs->h2d, ev_fwd[b], 0) == cudaSuccess;
+    ok = ok &&
+         cudaMemcpyAsync(slot + hc.x_off, xh + n0 * hc.x_img, nb * hc.x_img,
+                         cudaMemcpyHostToDevice, cs->h2d) == cudaSuccess &&
+         cudaMemcpyAsync(slot + hc.off_off, oh + n0 * hc.off_img, nb * hc.off_img,
+                         cudaMemcpyHostToDevice, cs->h2d) == cudaSuccess &&
+         cudaMemcpyAsync(slot + hc.mask_off, mh + n0 * hc.mask_img, nb * hc.mask_img,
+                         cudaMemcpyHostToDevice, cs->h2d) == cudaSuccess &&
+         cudaEventRecord(ev_in[b], cs->h2d) == cudaSuccess;
+    // forward (its y slot is free once the download of chunk i-2 has read it)
+    ok = ok && cudaStreamWaitEvent(st, ev_in[b], 0) == cudaSuccess;
+    if (i >= 2) ok = ok && cudaStreamWaitEvent(st, ev_out[b], 0) == cudaSuccess;
+    if (ok) {
+      dcnv2_desc d = *desc;
+      d.n = nb;
+      s = dcnv2_forward(&d, slot + hc.x_off, slot + hc.off_off, slot + hc.mask_off, weight, bias,
+                        slot + hc.y_off, ws + hc.fwd_off, hc.fwd_bytes, x_scale, w_scale, stream);
+      ok = s == DCNV2_OK && cudaEventRecord(ev_fwd[b], st) == cudaSuccess;
+    }
+    // download
+    ok = ok && cudaStreamWaitEvent(cs->d2h, ev_fwd[b], 0) == cudaSuccess &&
+         cudaMemcpyAsync(yh + n0 * hc.y_img, slot + hc.y_off, nb * hc.y_img,
+                         cudaMemcpyDeviceToHost, cs->d2h) == cudaSuccess &&
+         cudaEventRecord(ev_out[b], cs->d2h) == cudaSuccess;
+  }
+  // `stream` completes after every download
+  for (int b = 0; ok && b < 2 && b < i; ++b)
+    ok = cudaStreamWaitEvent(st, ev_out[b], 0) == cudaSuccess;
+  for (auto& e : ev) cudaEventDestroy(e);  // released once the work that uses them completes
+  if (!ok) {
+    cudaGetLastError();
+    return s != DCNV2_OK ? s : DCNV2_ERR_CUDA;
+  }
+  return DCNV2_OK;
+}
+
+// ---------------------------------------------------------------------------------------------
 // Allocation-free forward. Some callers cannot call cudaMalloc while they run (a fixed memory
 // plan, a latency-critical loop where an allocation would synchronise the device, a hard device
 // memory budget), so they cannot provide the workspace dcnv2_forward needs. For them the scratch

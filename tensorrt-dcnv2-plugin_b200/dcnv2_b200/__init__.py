@@ -5,8 +5,9 @@ if the library is missing, so no caller can silently run without the CUDA kernel
 """
 from .capi import DCNv2Error, DType, Math, Status, LIB_PATH  # noqa: F401
 from .plugin import (DCNv2Creator, DCNv2Plugin, FIELD_NAMES, PLUGIN_NAME,  # noqa: F401
-                     PLUGIN_NAMESPACE, PLUGIN_VERSION, dcnv2_forward, tensor_desc)
+                     PLUGIN_NAMESPACE, PLUGIN_VERSION, dcnv2_forward, dcnv2_forward_host,
+                     tensor_desc)
 
 __all__ = ["DCNv2Error", "DType", "Math", "Status", "DCNv2Creator", "DCNv2Plugin",
-           "dcnv2_forward", "tensor_desc", "PLUGIN_NAME", "PLUGIN_VERSION", "PLUGIN_NAMESPACE",
+           "dcnv2_forward", "dcnv2_forward_host", "tensor_desc", "PLUGIN_NAME", "PLUGIN_VERSION", "PLUGIN_NAMESPACE",
            "FIELD_NAMES", "LIB_PATH"]

@@ -80,6 +80,9 @@ def _load() -> ctypes.CDLL:
         "dcnv2_forward_static_scratch": (ctypes.c_int, [Dp, P, P, P, P, P, P, ctypes.c_float,
                                                         ctypes.c_float, P]),
         "dcnv2_read_device_error": (ctypes.c_int, [P, P, ctypes.POINTER(ctypes.c_int32)]),
+        "dcnv2_forward_host_workspace_size": (ctypes.c_size_t, [Dp, ctypes.c_int32]),
+        "dcnv2_forward_host": (ctypes.c_int, [Dp, P, P, P, P, P, P, P, ctypes.c_size_t,
+                                              ctypes.c_float, ctypes.c_float, ctypes.c_int32, P]),
         "dcnv2_uses_tensor_cores": (ctypes.c_int32, [Dp]),
         "dcnv2_launch_count": (ctypes.c_int32, [Dp]),
         "dcnv2_status_string": (ctypes.c_char_p, [ctypes.c_int]),
@@ -123,6 +126,7 @@ lib = _load()
 EXPORTED = (
     "dcnv2_output_shape", "dcnv2_workspace_size", "dcnv2_forward",
     "dcnv2_forward_static_scratch", "dcnv2_read_device_error",
+    "dcnv2_forward_host_workspace_size", "dcnv2_forward_host",
     "dcnv2_uses_tensor_cores", "dcnv2_launch_count", "dcnv2_status_string", "dcnv2_plugin_name",
     "dcnv2_plugin_version", "dcnv2_plugin_namespace", "dcnv2_plugin_field_names",
     "dcnv2_plugin_create", "dcnv2_plugin_clone", "dcnv2_plugin_destroy",
@@ -164,6 +168,20 @@ def forward_raw(desc: Desc, x, offset, mask, weight, bias, y, workspace, workspa
     """Raw C call with integer device addresses; returns the dcnv2_status value."""
     return int(lib.dcnv2_forward(ctypes.byref(desc), x, offset, mask, weight, bias, y, workspace,
                                  workspace_bytes, float(x_scale), float(w_scale), stream))
+
+
+def forward_host_workspace_size(desc: Desc, images_per_chunk: int = 0) -> int:
+    return int(lib.dcnv2_forward_host_workspace_size(ctypes.byref(desc), int(images_per_chunk)))
+
+
+def forward_host_raw(desc: Desc, x_host, offset_host, mask_host, weight, bias, y_host, workspace,
+                     workspace_bytes, x_scale=1.0, w_scale=1.0, images_per_chunk=0,
+                     stream=0) -> int:
+    """Raw call of the host-buffer forward (x, offset, mask, y host addresses; weight, bias and
+    workspace device addresses); returns the dcnv2_status value."""
+    return int(lib.dcnv2_forward_host(ctypes.byref(desc), x_host, offset_host, mask_host, weight,
+                                      bias, y_host, workspace, workspace_bytes, float(x_scale),
+                                      float(w_scale), int(images_per_chunk), stream))
 
 
 def read_device_error(workspace, stream=0) -> int:

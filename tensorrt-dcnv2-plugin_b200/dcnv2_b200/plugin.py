@@ -202,3 +202,49 @@ def dcnv2_forward(x, offset, mask, weight, bias=None, stride: int = 1, padding: 
     if st != Status.OK:
         raise DCNv2Error(st, "dcnv2_forward")
     return out
+
+
+def dcnv2_forward_host(x, offset, mask, weight, bias=None, stride: int = 1, padding: int = 1,
+                       dilation: int = 1, deformable_groups: int = 1, x_scale: float = 1.0,
+                       w_scale: float = 1.0, math: int = Math.DEFAULT, out=None, workspace=None,
+                       images_per_chunk: int = 0, stream=None, synchronize: bool = True):
+    """y = DCNv2(...) with x, offset, mask and y in host memory, through dcnv2_forward_host.
+
+    x, offset and mask are contiguous CPU tensors (page-locked for overlapped copies); weight and
+    bias are contiguous CUDA tensors. The batch is uploaded, computed and downloaded in chunks of
+    images with the copies overlapped. Returns the host output (pinned when allocated here);
+    with synchronize=False it is complete only once `stream` has completed.
+    """
+    import torch
+    dt = _dtype_of(x)
+    K = int(weight.shape[2])
+    N, C, H, W = (int(v) for v in x.shape)
+    O = int(weight.shape[0])
+    desc = capi.make_desc(N, C, H, W, O, K, stride, padding, dilation, deformable_groups, dt,
+                          math)
+    n, o, ho, wo = capi.output_shape(desc)
+    ydtype = torch.float16 if dt == DType.HALF else torch.float32
+    for t in (x, offset, mask):
+        if t.is_cuda or not t.is_contiguous():
+            raise ValueError("dcnv2_forward_host expects contiguous host tensors x, offset, mask")
+    for t in (weight,) + ((bias,) if bias is not None else ()):
+        if not t.is_cuda or not t.is_contiguous():
+            raise ValueError("dcnv2_forward_host expects contiguous CUDA weight and bias")
+    if out is None:
+        out = torch.empty((n, o, ho, wo), dtype=ydtype, pin_memory=True)
+    ws_bytes = capi.forward_host_workspace_size(desc, images_per_chunk)
+    if ws_bytes == 0:
+        raise DCNv2Error(Status.ERR_INVALID_ARG, "dcnv2_forward_host_workspace_size")
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=weight.device)
+    if stream is None:
+        stream = torch.cuda.current_stream(weight.device).cuda_stream
+    st = capi.forward_host_raw(desc, x.data_ptr(), offset.data_ptr(), mask.data_ptr(),
+                               weight.data_ptr(), bias.data_ptr() if bias is not None else None,
+                               out.data_ptr(), workspace.data_ptr(), workspace.numel(), x_scale,
+                               w_scale, images_per_chunk, stream)
+    if st != Status.OK:
+        raise DCNv2Error(st, "dcnv2_forward_host")
+    if synchronize:
+        torch.cuda.ExternalStream(stream, device=weight.device).synchronize()
+    return out

@@ -363,3 +363,29 @@ def test_tmem_a_kernel_matches_smem_a_kernel(shape, pair, monkeypatch):
     assert mean_rel(out["ta"][0], out["smem"][0]) <= 1e-4
     assert mean_rel(out["ta"][1], out["smem"][1]) <= 1e-4
     np.testing.assert_allclose(out["ta"][2], out["smem"][2], rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("chunk", [0, 1, 2, 5])
+def test_host_buffer_forward_matches_device_forward(chunk):
+    """dcnv2_forward_host (x, offset, mask, y on the host; uploads, forwards and downloads of
+    image chunks overlapped) gives bit-identical results to dcnv2_forward, for every precision
+    and for chunk sizes that leave a ragged last chunk."""
+    from dcnv2_b200 import dcnv2_forward_host
+    fx = random_case(n=5, c=64, o=48, h=20, w=18, ostd=0.6, outl=0.02, seed=11)
+    cases = [(torch.float32, {}), (torch.float16, {})]
+    xq, xs, wq, ws = quantized(fx)
+    for dt, kw in cases:
+        host = [torch.from_numpy(fx[k]).to(dt).contiguous().pin_memory()
+                for k in ("x", "offset", "mask")]
+        w = cuda(fx["weight"], dt)
+        b = cuda(fx["bias"], dt)
+        ref = dcnv2_forward(*[h.to(DEV) for h in host], w, b, **attrs(fx))
+        y = dcnv2_forward_host(*host, w, b, images_per_chunk=chunk, **attrs(fx))
+        assert torch.equal(y, ref.cpu())
+    host = [torch.from_numpy(np.ascontiguousarray(xq)).pin_memory(),
+            torch.from_numpy(fx["offset"]).pin_memory(), torch.from_numpy(fx["mask"]).pin_memory()]
+    w8, b32 = cuda(wq, torch.int8), cuda(fx["bias"], torch.float32)
+    ref8 = dcnv2_forward(*[h.to(DEV) for h in host], w8, b32, x_scale=xs, w_scale=ws, **attrs(fx))
+    y8 = dcnv2_forward_host(*host, w8, b32, x_scale=xs, w_scale=ws, images_per_chunk=chunk,
+                            **attrs(fx))
+    assert torch.equal(y8, ref8.cpu())
