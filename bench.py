@@ -353,16 +353,55 @@ def torchvision_cpu(inp_cpu, seconds: float):
 
 
 # ---------------------------------------------------------------- arms
+L2_BYTES = 126 * 1024 * 1024
+
+
+def time_steps_flushed(runs, stream, steps, dist, flush):
+    """Per-step CUDA-event timing with the L2 flushed (a write larger than L2) before each step;
+    the flush is outside the events. Returns ms per step and ms per part of a step."""
+    torch.cuda.synchronize()
+    dist.barrier()
+    per_part = np.zeros(len(runs))
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(runs) + 1)]
+           for _ in range(steps)]
+    for i in range(steps):
+        with torch.cuda.stream(stream):
+            flush.add_(1)
+        for k, run in enumerate(runs):
+            evs[i][k].record(stream)
+            run(stream.cuda_stream)
+        evs[i][len(runs)].record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    for i in range(steps):
+        per_part += [evs[i][k].elapsed_time(evs[i][k + 1]) for k in range(len(runs))]
+    per_part /= steps
+    return float(per_part.sum()), per_part
+
+
 def run_ours(args, dist):
     device = torch.device(f"cuda:{dist.local}")
     torch.cuda.set_device(device)
     stream = torch.cuda.Stream(device)
     from dcnv2_b200 import capi
-    inp_cpu = wl.workload(args.workload, seed=1000 * dist.rank)
-    inp = inp_cpu.to(device)
-    ws, out = alloc_for(inp, device)
-    desc, ptrs, run = step_fn(inp, ws, out)
-    launches = capi.launch_count(desc)
+    parts_cpu = wl.workload_parts(args.workload, seed=1000 * dist.rank)
+    parts = [p.to(device) for p in parts_cpu]
+    bufs = [alloc_for(p, device) for p in parts]
+    fns = [step_fn(p, ws, out) for p, (ws, out) in zip(parts, bufs)]
+    runs = [f[2] for f in fns]
+    launches = sum(capi.launch_count(f[0]) for f in fns)
+    # the dominant layer (most FLOPs) carries the roofline, the CPU baseline and e2e details
+    dom = max(range(len(parts)), key=lambda i: parts[i].layer.flops)
+    inp, inp_cpu = parts[dom], parts_cpu[dom]
+    (ws, out), (desc, _, _) = bufs[dom], fns[dom]
+    step_bytes = sum(p.input_bytes + p.output_bytes for p in parts)
+    flush = None
+    if step_bytes < 2 * L2_BYTES:  # small working set: flush L2 between timed steps
+        flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=device)
+
+    def run_all(st):
+        for r in runs:
+            r(st)
 
     try:  # nvidia-smi addresses the physical GPU; torch's index may be remapped
         gpu_id = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
@@ -371,45 +410,53 @@ def run_ours(args, dist):
     clocks = ClockSampler(gpu_id)
     # warm-up, then the timed region with clock sampling around it
     for _ in range(args.warmup):
-        run(stream.cuda_stream)
+        run_all(stream.cuda_stream)
     torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
-    ms = time_steps(run, stream, args.steps, 0, dist)
+    if flush is None:
+        ms = time_steps(run_all, stream, args.steps, 0, dist)
+        part_ms = None
+    else:
+        ms, part_ms = time_steps_flushed(runs, stream, args.steps, dist, flush)
     clk = clocks.stop()
     ms = dist.max(ms)
 
-    flops = flops_of(inp)
+    flops = sum(p.layer.flops for p in parts)
+    int8 = inp.precision == "int8"
     value = flops * dist.world / (ms * 1e-3) / 1e12
 
     # per-kernel breakdown (live CUDA events between launches), dominant kernel roofline
     per = kernel_breakdown(inp, ws, out, stream, min(args.steps, 200))
-    kname = {1: "dcnv2_fused_kernel", 2: "dcnv2_f32_exact_kernel", 0: "dcnv2_simt_kernel"}[
-        capi.uses_tensor_cores(desc)]
+    kname = capi.main_kernel(desc)
     main_ms = float(per[-1])
     peak_tf, peak_hbm, peak_kind = peaks()
-    tensor_peak = peak_tf * (2.0 if inp.precision == "int8" else 1.0)
+    tensor_peak = peak_tf * (2.0 if int8 else 1.0)
     if inp.precision == "fp32":
         tensor_peak = None
-    achieved = flops / (main_ms * 1e-3) / 1e12
+    achieved = inp.layer.flops / (main_ms * 1e-3) / 1e12
     traffic = traffic_for(args.workload, kname)
+    unit = "TOP/s" if int8 else "TFLOP/s"
     if tensor_peak:
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(tensor_peak, 1),
-                "unit": "TFLOP/s", "frac": round(achieved / tensor_peak, 4),
+                "unit": unit, "frac": round(achieved / tensor_peak, 4),
                 "traffic": traffic, "kernel": kname, "kernel_ms": round(main_ms, 4),
                 "peak_source": f"{peak_kind} bf16 dense"
-                               + (" x2 (int8 dense rate)" if inp.precision == "int8" else "")}
+                               + (" x2 (int8 dense rate)" if int8 else "")}
     else:
         roof = {"bound": "fp32 CUDA cores", "achieved": round(achieved, 1), "peak": None,
-                "unit": "TFLOP/s", "frac": None, "traffic": traffic, "kernel": kname,
+                "unit": unit, "frac": None, "traffic": traffic, "kernel": kname,
                 "kernel_ms": round(main_ms, 4)}
     roof["launch_ms"] = [round(float(v), 4) for v in per]
     alg_bytes = inp.input_bytes + inp.output_bytes
     roof["hbm_alg_gbs"] = round(alg_bytes / (float(per.sum()) * 1e-3) / 1e9, 1)
 
-    # end to end through the plugin with host buffers
-    e2e_ms, h2d, d2h = e2e_measure(inp_cpu, device, stream, args.e2e_steps, dist)
-    e2e = {"value": round(flops * dist.world / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+    # end to end through the C ABI with host buffers
+    e2e_ms, h2d, d2h = 0.0, 0, 0
+    for p in parts_cpu:
+        m, i_b, o_b = e2e_measure(p, device, stream, args.e2e_steps, dist)
+        e2e_ms, h2d, d2h = e2e_ms + m, h2d + i_b, d2h + o_b
+    e2e = {"value": round(flops * dist.world / (e2e_ms * 1e-3) / 1e12, 3), "unit": unit,
            "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
     secondary = {}
@@ -430,7 +477,7 @@ def run_ours(args, dist):
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         v, sample, thr = cpu_baseline(inp_cpu, args.cpu_seconds)
-        cpu = {"value": round(v, 5), "unit": "TFLOP/s", "cores": thr, "kind": "port",
+        cpu = {"value": round(v, 5), "unit": unit, "cores": thr, "kind": "port",
                "sample": sample}
         tv = torchvision_cpu(inp_cpu, min(args.cpu_seconds, 20.0))
         if tv:
@@ -438,22 +485,35 @@ def run_ours(args, dist):
 
     if dist.rank == 0:
         L = inp.layer
+        if args.workload == "fp16_n64_256c_64":
+            metric = "DCNv2 fwd TFLOP/s (256ch 64x64 3x3) fp16, 1-8 B200"
+        else:
+            metric = f"DCNv2 fwd {unit} ({args.workload}), 1-8 B200"
+        l2 = ("step working set exceeds L2 (no flush)" if flush is None else
+              "L2 flushed before every timed step (a 252 MB write outside the timed events)")
+        config = {"workload": args.workload, "batch_per_gpu": L.n,
+                  "global_batch": L.n * dist.world, "c": L.c, "out_c": L.out_c,
+                  "hw": [L.h, L.w], "kernel": L.kernel, "stride": L.stride,
+                  "padding": L.padding, "dilation": L.dilation,
+                  "deformable_groups": L.groups, "parallelism": f"batch-shard x{dist.world}",
+                  "l2": l2}
+        if len(parts) > 1:
+            config["levels_hw"] = [p.layer.h for p in parts]
         line = {
-            "metric": "DCNv2 fwd TFLOP/s (256ch 64x64 3x3) fp16, 1-8 B200",
-            "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": dist.world,
+            "metric": metric,
+            "value": round(value, 2), "unit": unit, "n_gpus": dist.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": inp.precision, "data": "synthetic (seeded torch.Generator, see workloads.py)",
-            "config": {"workload": args.workload, "batch_per_gpu": L.n,
-                       "global_batch": L.n * dist.world, "c": L.c, "out_c": L.out_c,
-                       "hw": [L.h, L.w], "kernel": L.kernel, "stride": L.stride,
-                       "padding": L.padding, "dilation": L.dilation,
-                       "deformable_groups": L.groups, "parallelism": f"batch-shard x{dist.world}",
-                       "l2": "inputs exceed L2 (x and y 134 MB each), no flush"},
+            "config": config,
             "images_per_s": round(L.n * dist.world / (ms * 1e-3), 1),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
             "gpu_launches": launches * args.steps, "secondary": secondary or None,
         }
+        if part_ms is not None and len(parts) > 1:
+            line["levels"] = [{"hw": p.layer.h, "ms": round(float(m), 4),
+                               "tflops": round(p.layer.flops / (m * 1e-3) / 1e12, 1)}
+                              for p, m in zip(parts, part_ms)]
         print(json.dumps(line), flush=True)
 
 

@@ -31,6 +31,12 @@ DCNV2_API dcnv2_status dcnv2_diag_forward_events(const dcnv2_desc* desc, const v
                                                  dcnv2_stream_t stream, void* const* events,
                                                  int32_t n_events);
 
+/* Name of the last (main) kernel dcnv2_forward launches for this desc: "dcnv2_fused_ta_kernel"
+ * (tensor cores, A operand in TMEM), "dcnv2_fused_kernel" (tensor cores, A in shared memory),
+ * "dcnv2_f32_exact_kernel" or "dcnv2_simt_kernel"; NULL on a bad desc. For labelling
+ * measurements and matching profiler output. */
+DCNV2_API const char* dcnv2_diag_main_kernel(const dcnv2_desc* desc);
+
 #ifdef __cplusplus
 }
 #endif

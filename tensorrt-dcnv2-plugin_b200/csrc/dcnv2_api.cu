@@ -691,6 +691,16 @@ int32_t dcnv2_uses_tensor_cores(const dcnv2_desc* desc) {
   return p.kind;
 }
 
+const char* dcnv2_diag_main_kernel(const dcnv2_desc* desc) {
+  Plan p;
+  if (make_plan(desc, &p) != DCNV2_OK) return nullptr;
+  switch (p.kind) {
+    case KIND_TCGEN05: return p.ta ? "dcnv2_fused_ta_kernel" : "dcnv2_fused_kernel";
+    case KIND_F32_EXACT: return "dcnv2_f32_exact_kernel";
+    default: return "dcnv2_simt_kernel";
+  }
+}
+
 int32_t dcnv2_launch_count(const dcnv2_desc* desc) {
   Plan p;
   if (make_plan(desc, &p) != DCNV2_OK) return 0;

@@ -85,6 +85,7 @@ def _load() -> ctypes.CDLL:
                                               ctypes.c_float, ctypes.c_float, ctypes.c_int32, P]),
         "dcnv2_uses_tensor_cores": (ctypes.c_int32, [Dp]),
         "dcnv2_launch_count": (ctypes.c_int32, [Dp]),
+        "dcnv2_diag_main_kernel": (ctypes.c_char_p, [Dp]),
         "dcnv2_status_string": (ctypes.c_char_p, [ctypes.c_int]),
         "dcnv2_plugin_name": (ctypes.c_char_p, []),
         "dcnv2_plugin_version": (ctypes.c_char_p, []),
@@ -133,6 +134,7 @@ EXPORTED = (
     "dcnv2_plugin_serialize", "dcnv2_plugin_nb_outputs", "dcnv2_plugin_output_dtype",
     "dcnv2_plugin_output_shape", "dcnv2_plugin_supports_format", "dcnv2_plugin_workspace_size",
     "dcnv2_plugin_enqueue", "dcnv2_diag_timeout_selftest", "dcnv2_diag_forward_events",
+    "dcnv2_diag_main_kernel",
 )
 
 
@@ -157,6 +159,14 @@ def workspace_size(desc: Desc) -> int:
 def uses_tensor_cores(desc: Desc) -> int:
     """1 = fused tcgen05 kernel, 2 = fused fp32-exact CUDA-core kernel, 0 = per-output kernel."""
     return int(lib.dcnv2_uses_tensor_cores(ctypes.byref(desc)))
+
+
+def main_kernel(desc: Desc) -> str:
+    """Name of the main kernel dcnv2_forward launches for this desc."""
+    name = lib.dcnv2_diag_main_kernel(ctypes.byref(desc))
+    if name is None:
+        raise DCNv2Error(Status.ERR_INVALID_ARG, "dcnv2_diag_main_kernel")
+    return name.decode()
 
 
 def launch_count(desc: Desc) -> int:

@@ -136,7 +136,7 @@ def make_layer_inputs(layer: Layer, precision: str, offset_std: float, mask_mean
 
 
 WORKLOADS = ("fp32_n1_256c_64", "fp16_n64_256c_64", "int8_n64_256c_64", "fpn_fp16_b32",
-             "big_512c_128_dg8")
+             "big_512c_128_dg8", "big_512c_128_dg8_int8")
 
 
 def workload(name: str, n: Optional[int] = None, precision: Optional[str] = None,
@@ -155,10 +155,19 @@ def workload(name: str, n: Optional[int] = None, precision: Optional[str] = None
         s = level or 64
         return make_layer_inputs(Layer(n or 32, 256, s, s, 256), "fp16", 0.1, 3.0, 0.5,
                                  seed=seed + s)
-    if name == "big_512c_128_dg8":
+    if name in ("big_512c_128_dg8", "big_512c_128_dg8_int8"):
+        prec = precision or ("int8" if name.endswith("int8") else "fp16")
         return make_layer_inputs(Layer(n or 16, 512, 128, 128, 512, 3, 1, 2, 2, 8),
-                                 precision or "fp16", 2.0, 0.0, 1.0, seed=seed)
+                                 prec, 2.0, 0.0, 1.0, seed=seed)
     raise KeyError(name)
 
 
 FPN_LEVELS = (64, 32, 16, 8, 4)
+
+
+def workload_parts(name: str, n: Optional[int] = None, seed: int = 0):
+    """The layers one step of a workload runs: the five FPN levels (P3..P7) of fpn_fp16_b32, a
+    single layer otherwise."""
+    if name == "fpn_fp16_b32":
+        return [workload(name, n=n, level=s, seed=seed) for s in FPN_LEVELS]
+    return [workload(name, n=n, seed=seed)]
