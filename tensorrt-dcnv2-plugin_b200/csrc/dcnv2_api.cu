@@ -439,7 +439,15 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
     const int HW = p.H * p.W;
     dim3 grid(static_cast<unsigned>(cdiv(HW, TILE)), static_cast<unsigned>(cdiv(p.C, TILE)),
               static_cast<unsigned>(p.N));
-    if (grid.z > 65535u) {
+    const bool i8_tiles = sizeof(XT) == 1 && p.C % 128 == 0 && HW % 128 == 0 &&
+                          (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                          (reinterpret_cast<uintptr_t>(x_nhwc) & 15u) == 0;
+    if (i8_tiles && grid.z <= 65535u) {
+      mk.mark(st);
+      nchw_to_nhwc_i8_kernel<<<dim3(static_cast<unsigned>(HW / 128), static_cast<unsigned>(p.C / 128),
+                                    static_cast<unsigned>(p.N)), 256, 0, st>>>(
+          reinterpret_cast<const int8_t*>(x), reinterpret_cast<int8_t*>(x_nhwc), p.C, HW);
+    } else if (grid.z > 65535u) {
       // Split large batches into launches of at most 65535 images.
       for (int n0 = 0; n0 < p.N; n0 += 65535) {
         const int nb = p.N - n0 < 65535 ? p.N - n0 : 65535;

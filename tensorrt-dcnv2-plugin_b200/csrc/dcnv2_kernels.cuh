@@ -1069,6 +1069,50 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const T* __restrict__
   }
 }
 
+// int8 NCHW -> NHWC for C % 128 == 0 and H*W % 128 == 0 (16-byte aligned pointers): a tile of 128
+// channels x 128 pixels. Channel c of the tile sits in shared row (c % 16) * 8 + c / 16 (rows of
+// 36 words), so that the 8 channel groups a warp reads at once fall in different bank groups.
+// Each thread turns 16 words (16 channels x 4 pixels) into 4 pixels x 16 channels with byte
+// permutes (4x4 byte transposes) and writes four 16-byte vectors; the 8 threads of one pixel
+// write its 128 channels contiguously.
+__global__ void __launch_bounds__(256) nchw_to_nhwc_i8_kernel(const int8_t* __restrict__ x,
+                                                              int8_t* __restrict__ xt, int C,
+                                                              int HW) {
+  constexpr int kRowWords = 36;
+  __shared__ __align__(16) uint32_t tile[128 * kRowWords];
+  const int n = blockIdx.z;
+  const int c0 = blockIdx.y * 128, p0 = blockIdx.x * 128;
+  const int8_t* xs = x + static_cast<size_t>(n) * C * HW;
+  int8_t* xd = xt + static_cast<size_t>(n) * C * HW;
+  const int t = threadIdx.x;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = (t >> 3) + 32 * i, q = t & 7;  // channel of the tile, 16-pixel chunk
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(xs + static_cast<size_t>(c0 + c) * HW + p0) + q);
+    const int row = (c & 15) * 8 + (c >> 4);
+    *reinterpret_cast<uint4*>(&tile[row * kRowWords + 4 * q]) = v;
+  }
+  __syncthreads();
+  const int cg = t & 7, pg = t >> 3;  // channels 16*cg.., pixels 4*pg..
+  uint32_t o[4][4];                   // o[pixel j][word m] = channels 16cg+4m..+3 of pixel 4pg+j
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) w[k] = tile[((4 * m + k) * 8 + cg) * kRowWords + pg];
+    const uint32_t t0 = __byte_perm(w[0], w[1], 0x5140), t1 = __byte_perm(w[0], w[1], 0x7362);
+    const uint32_t t2 = __byte_perm(w[2], w[3], 0x5140), t3 = __byte_perm(w[2], w[3], 0x7362);
+    o[0][m] = __byte_perm(t0, t2, 0x5410);
+    o[1][m] = __byte_perm(t0, t2, 0x7632);
+    o[2][m] = __byte_perm(t1, t3, 0x5410);
+    o[3][m] = __byte_perm(t1, t3, 0x7632);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4*>(xd + static_cast<size_t>(p0 + 4 * pg + j) * C + c0 + 16 * cg) =
+        make_uint4(o[j][0], o[j][1], o[j][2], o[j][3]);
+}
+
 // ------------------------------------------------------------------ pre-pass: weight pack
 // Writes, for every (cout chunk, K-block), the B operand tile exactly as it must sit in shared
 // memory: row o (output channel), 16-byte chunk jc at chunk jc ^ (o % 8) of the 128-byte row.

@@ -13,11 +13,10 @@
 // Roles (576 threads; 18 warps leave each thread 96 registers):
 //   warp 0       producer: bulk copy of each K-block's pre-swizzled weight tile (B ring, smem)
 //   warp 1       MMA issuer (lane 0): tcgen05.mma kind::f16 / kind::i8, A from TMEM, B from smem
-//   warps 2-9    epilogue (two per TMEM lane quadrant, half of the columns each): tcgen05.ld of
-//                the accumulator, + bias (x x_scale*w_scale for int8), stores of y (two pixels
-//                per store where the layout allows)
-//   warps 10-17  samplers: warp w fills TMEM lane quadrant w % 4 (32 pixels, thread = pixel),
-//                whole 128-byte rows of the K-blocks of taps t = (w - 10) / 4 (mod 2)
+//   warps 2-5    epilogue: tcgen05.ld of the accumulator, + bias (x x_scale*w_scale for int8),
+//                stores of y (two pixels per store where the layout allows)
+//   warps 6-17   samplers: warp w fills TMEM lane quadrant w % 4 (32 pixels, thread = pixel),
+//                whole 128-byte rows of the K-blocks of taps t = (w - 6) / 4 (mod 3)
 // The x window is stored linearly (128 bytes per pixel, so 16-byte chunk c of any pixel sits in
 // bank group c). In the 3x3 fp16 fast path lane i reads chunk h ^ (i % 8) at step h: the 8 lanes
 // of each 128-bit load phase hit 8 different bank groups whatever the offsets, and a register
@@ -41,15 +40,9 @@ template <int PREC> struct TaLayout {
 };
 constexpr uint32_t kTaTmemCols = 512;
 constexpr int kTaMaxBStages = 8;
-// Warp roles: 0 producer, 1 MMA, 2..9 epilogue (two per TMEM lane quadrant, 128 accumulator
-// columns each), 10..17 samplers (two per quadrant: tap groups t even / t odd). 18 warps leave
-// each thread 96 registers (five warps per SM sub-partition).
-constexpr int kTaEpiWarp0 = 2;
-constexpr int kTaEpiWarps = 8;
-constexpr int kTaTapGroups = 2;        // sampler warps per TMEM lane quadrant
-constexpr int kTaSampWarp0 = kTaEpiWarp0 + kTaEpiWarps;
+constexpr int kTaTapGroups = 3;        // sampler warps per TMEM lane quadrant
 constexpr int kTaSampWarps = 4 * kTaTapGroups;
-constexpr int kTaThreads = (kTaSampWarp0 + kTaSampWarps) * 32;  // 576
+constexpr int kTaThreads = (kSampWarp0 + kTaSampWarps) * 32;  // 576: 18 warps, 96 registers
 
 struct TaMmaParams {
   uint32_t b_base, b_stage_bytes, tmem_base;
@@ -237,7 +230,7 @@ __global__ void __launch_bounds__(kTaThreads, 1)
       ptx::mbar_init(b_empty + 8 * s, 1);
     }
     ptx::mbar_init(tfull, 1);
-    ptx::mbar_init(tempty, PAIR ? 2 * kTaEpiWarps : kTaEpiWarps);
+    ptx::mbar_init(tempty, PAIR ? 2 * kNumEpiWarps : kNumEpiWarps);
     ptx::mbar_init(drain, 1);
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(win_full + 8 * i, 1);
@@ -336,7 +329,7 @@ __global__ void __launch_bounds__(kTaThreads, 1)
       }
       wait_bar(drain, 0, wc, DCNV2_DEVERR_TIMEOUT_DRAIN);
     }
-  } else if (warp < kTaSampWarp0) {
+  } else if (warp < kSampWarp0) {
     // ------------------------------------------------------------ epilogue
     // Per 16 accumulator columns: tcgen05.ld (the next block's load overlaps this block's
     // stores), + bias from shared memory (staged at kernel start; a global load per column
@@ -344,9 +337,6 @@ __global__ void __launch_bounds__(kTaThreads, 1)
     // small), convert, store. Lanes 2i and 2i+1 swap one value per channel pair so that each
     // store covers two pixels, when every pixel pair starts on an aligned address.
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    // the two warps of a quadrant take halves of the columns (64-column aligned ranges)
-    const int eh = (warp - kTaEpiWarp0) >> 2;
-    const int hcols = ((args.n_mma / 2) + 63) & ~63;
     const bool paired = (args.P % 2) == 0 &&
                         (reinterpret_cast<uintptr_t>(args.y) % (2 * sizeof(YT))) == 0;
     const bool staged = args.cchunks == 1;
@@ -364,8 +354,6 @@ __global__ void __launch_bounds__(kTaThreads, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
       const int o_chunk = cc * args.n_mma;
       const int ncols = args.O - o_chunk < args.n_mma ? args.O - o_chunk : args.n_mma;
-      const int c_beg = eh * hcols;
-      const int c_end = ncols < c_beg + hcols ? ncols : c_beg + hcols;  // may be empty
       YT* yimg = reinterpret_cast<YT*>(args.y) + static_cast<size_t>(img) * args.O * args.P;
       auto block = [&](const uint32_t (&r)[16], int col) {
         const int o0 = o_chunk + col;
@@ -449,14 +437,14 @@ __global__ void __launch_bounds__(kTaThreads, 1)
           }
           ptx::tmem_st_32x32b_x8(park + col / 2, h);
         };
-        if (c_beg < c_end) ptx::tmem_ld_32x32b_x16(taddr + c_beg, ra);
-        for (int col = c_beg; col < c_end; col += 32) {  // warp-uniform bounds
+        ptx::tmem_ld_32x32b_x16(taddr, ra);
+        for (int col = 0; col < ncols; col += 32) {  // warp-uniform bounds
           ptx::tmem_wait_ld_regs(ra);
-          if (col + 16 < c_end) ptx::tmem_ld_32x32b_x16(taddr + col + 16, rb);
+          if (col + 16 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 16, rb);
           drain(ra, col);
-          if (col + 16 < c_end) {
+          if (col + 16 < ncols) {
             ptx::tmem_wait_ld_regs(rb);
-            if (col + 32 < c_end) ptx::tmem_ld_32x32b_x16(taddr + col + 32, ra);
+            if (col + 32 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 32, ra);
             drain(rb, col + 16);
           }
         }
@@ -485,26 +473,26 @@ __global__ void __launch_bounds__(kTaThreads, 1)
             }
           }
         };
-        if (c_beg < c_end) ptx::tmem_ld_32x32b_x16(park + c_beg / 2, ra);
-        for (int col = c_beg; col < c_end; col += 64) {  // 32 channels per load
+        ptx::tmem_ld_32x32b_x16(park, ra);
+        for (int col = 0; col < ncols; col += 64) {  // 32 channels per load
           ptx::tmem_wait_ld_regs(ra);
-          if (col + 32 < c_end) ptx::tmem_ld_32x32b_x16(park + col / 2 + 16, rb);
+          if (col + 32 < ncols) ptx::tmem_ld_32x32b_x16(park + col / 2 + 16, rb);
           store(ra, col);
-          if (col + 32 < c_end) {
+          if (col + 32 < ncols) {
             ptx::tmem_wait_ld_regs(rb);
-            if (col + 64 < c_end) ptx::tmem_ld_32x32b_x16(park + col / 2 + 32, ra);
+            if (col + 64 < ncols) ptx::tmem_ld_32x32b_x16(park + col / 2 + 32, ra);
             store(rb, col + 32);
           }
         }
       } else {
-        if (c_beg < c_end) ptx::tmem_ld_32x32b_x16(taddr + c_beg, ra);
-        for (int col = c_beg; col < c_end; col += 32) {  // warp-uniform bounds
+        ptx::tmem_ld_32x32b_x16(taddr, ra);
+        for (int col = 0; col < ncols; col += 32) {  // warp-uniform bounds
           ptx::tmem_wait_ld_regs(ra);
-          if (col + 16 < c_end) ptx::tmem_ld_32x32b_x16(taddr + col + 16, rb);
+          if (col + 16 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 16, rb);
           block(ra, col);
-          if (col + 16 < c_end) {
+          if (col + 16 < ncols) {
             ptx::tmem_wait_ld_regs(rb);
-            if (col + 32 < c_end) ptx::tmem_ld_32x32b_x16(taddr + col + 32, ra);
+            if (col + 32 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 32, ra);
             block(rb, col + 16);
           }
         }
@@ -513,17 +501,17 @@ __global__ void __launch_bounds__(kTaThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ samplers
-    // Thread = A row (pixel) mrow = 32 * (warp % 4) + lane of the CTA's 128. The warps of a lane
-    // quadrant split the taps: warp j = (warp - kTaSampWarp0) / 4 takes the K-blocks of taps
-    // t = j (mod kTaTapGroups) and writes whole 128-byte rows (all 8 chunks: 32 TMEM columns) of
-    // them, so it needs the geometry of its own taps only. Per K-block a thread reads the 4 corners of each
+    // Thread = A row (pixel) mrow = 32 * (warp % 4) + lane of the CTA's 128. The 3 warps of a lane
+    // quadrant split the taps: warp j = (warp - kSampWarp0) / 4 takes the K-blocks of taps
+    // t = j (mod 3) and writes whole 128-byte rows (all 8 chunks: 32 TMEM columns) of them, so it
+    // needs the geometry of its own taps only. Per K-block a thread reads the 4 corners of each
     // chunk (32 x 16 bytes), mixes them and stores its row with one tcgen05.st; the store of a
     // K-block is published after the next K-block's loads and mix (one store in flight per warp).
     constexpr int EPC = TR::kChunkElems, KC = TR::kBlockElems, EB = TR::kElemBytes;
     constexpr bool kFast = (!PRECISE && KT > 0);
     constexpr int kMyTaps = kFast ? (KT + kTaTapGroups - 1) / kTaTapGroups : 1;
     constexpr uint32_t kNoWin = 0xFFFFu;
-    const int sw = warp - kTaSampWarp0;
+    const int sw = warp - kSampWarp0;
     const int q = warp & 3;
     const int j = sw >> 2;  // tap group
     const int mrow = q * 32 + lane;
