@@ -1209,7 +1209,8 @@ __global__ void __launch_bounds__(kXThreads, 2) dcnv2_f32_exact_kernel(const Exa
   const bool pvalid = p < a.P;
   const int pc = pvalid ? p : 0;
   const int oh = pc / a.Wo, ow = pc - oh * a.Wo;
-  // compute role: pixels ty*4 .. +4, output channels tx*8 .. +8
+  // compute role: pixels ty*4 .. +4, output channels tx*4 .. +4 and 64 + tx*4 .. +4 (the two
+  // float4 reads of a half-warp cover 256 contiguous bytes: no bank conflicts)
   const int ty = tid >> 4, tx = tid & 15;
   const float* ximg = a.x_nhwc + static_cast<size_t>(img) * a.H * a.W * a.C;
   const float* wct = a.wplain + static_cast<size_t>(ct) * a.numKB * kXK * kXCo;
@@ -1291,8 +1292,8 @@ __global__ void __launch_bounds__(kXThreads, 2) dcnv2_f32_exact_kernel(const Exa
 #pragma unroll 8
     for (int k = 0; k < kXK; ++k) {
       const float4 av = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4]);
-      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 8]);
-      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 8 + 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][k][kXCo / 2 + tx * 4]);
       const float ar[4] = {av.x, av.y, av.z, av.w};
       const float br[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
@@ -1306,7 +1307,7 @@ __global__ void __launch_bounds__(kXThreads, 2) dcnv2_f32_exact_kernel(const Exa
   float* yimg = a.y + static_cast<size_t>(img) * a.O * a.P;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const int o = ct * kXCo + tx * 8 + j;
+    const int o = ct * kXCo + (j < 4 ? tx * 4 + j : kXCo / 2 + tx * 4 + (j - 4));
     if (o >= a.O) continue;
     const float bo = a.bias ? __ldg(a.bias + o) : 0.f;
 #pragma unroll
