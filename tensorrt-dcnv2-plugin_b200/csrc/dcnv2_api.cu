@@ -442,7 +442,15 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
     const bool i8_tiles = sizeof(XT) == 1 && p.C % 128 == 0 && HW % 128 == 0 &&
                           (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
                           (reinterpret_cast<uintptr_t>(x_nhwc) & 15u) == 0;
-    if (i8_tiles && grid.z <= 65535u) {
+    const bool f16_tiles = sizeof(XT) == 2 && p.C % 64 == 0 && HW % 128 == 0 &&
+                           (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                           (reinterpret_cast<uintptr_t>(x_nhwc) & 15u) == 0;
+    if (f16_tiles && grid.z <= 65535u) {
+      mk.mark(st);
+      nchw_to_nhwc_f16_kernel<<<dim3(static_cast<unsigned>(HW / 128), static_cast<unsigned>(p.C / 64),
+                                     static_cast<unsigned>(p.N)), 256, 0, st>>>(
+          reinterpret_cast<const __half*>(x), reinterpret_cast<__half*>(x_nhwc), p.C, HW);
+    } else if (i8_tiles && grid.z <= 65535u) {
       mk.mark(st);
       nchw_to_nhwc_i8_kernel<<<dim3(static_cast<unsigned>(HW / 128), static_cast<unsigned>(p.C / 128),
                                     static_cast<unsigned>(p.N)), 256, 0, st>>>(

@@ -1113,6 +1113,49 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_i8_kernel(const int8_t* __re
         make_uint4(o[j][0], o[j][1], o[j][2], o[j][3]);
 }
 
+// fp16 NCHW -> NHWC for C % 64 == 0 and H*W % 128 == 0 (16-byte aligned pointers): a tile of 64
+// channels x 128 pixels. A shared word holds two pixels of one channel; channel c of the tile sits
+// in shared row (c % 8) * 8 + c / 8 (rows of 68 words), so the 8 channel groups a warp reads at
+// once fall in different bank groups. Each thread turns 8 words (8 channels x 2 pixels) into
+// 2 pixels x 8 channels with byte permutes and writes two 16-byte vectors; the 8 threads of one
+// pixel write its 64 channels contiguously.
+__global__ void __launch_bounds__(256) nchw_to_nhwc_f16_kernel(const __half* __restrict__ x,
+                                                               __half* __restrict__ xt, int C,
+                                                               int HW) {
+  constexpr int kRowWords = 68;
+  __shared__ __align__(16) uint32_t tile[64 * kRowWords];
+  const int n = blockIdx.z;
+  const int c0 = blockIdx.y * 64, p0 = blockIdx.x * 128;
+  const __half* xs = x + static_cast<size_t>(n) * C * HW;
+  __half* xd = xt + static_cast<size_t>(n) * C * HW;
+  const int t = threadIdx.x;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = (t >> 4) + 16 * i, q = t & 15;  // channel of the tile, 8-pixel chunk
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(xs + static_cast<size_t>(c0 + c) * HW + p0) + q);
+    const int row = (c & 7) * 8 + (c >> 3);
+    *reinterpret_cast<uint4*>(&tile[row * kRowWords + 4 * q]) = v;
+  }
+  __syncthreads();
+  const int cg = t & 7;  // channels 8*cg .. 8*cg+7
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int pp = (t >> 3) + 32 * r;  // pixel pair: pixels 2*pp, 2*pp+1
+    uint32_t w[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) w[k] = tile[(k * 8 + cg) * kRowWords + pp];
+    uint32_t lo[4], hi[4];  // pixel 2pp (low halves) and 2pp+1 (high halves), channel pairs
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      lo[m] = __byte_perm(w[2 * m], w[2 * m + 1], 0x5410);
+      hi[m] = __byte_perm(w[2 * m], w[2 * m + 1], 0x7632);
+    }
+    __half* dst = xd + static_cast<size_t>(p0 + 2 * pp) * C + c0 + 8 * cg;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(dst + C) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  }
+}
+
 // ------------------------------------------------------------------ pre-pass: weight pack
 // Writes, for every (cout chunk, K-block), the B operand tile exactly as it must sit in shared
 // memory: row o (output channel), 16-byte chunk jc at chunk jc ^ (o % 8) of the 128-byte row.
