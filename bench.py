@@ -454,9 +454,11 @@ def run_ours(args, dist):
     achieved = inp.layer.flops / (main_ms * 1e-3) / 1e12
     traffic = traffic_for(args.workload, kname)
     unit = "TOP/s" if int8 else "TFLOP/s"
+    spec_peak = 4500.0 if int8 else 2250.0  # B200 dense tensor peaks (no 2:4 sparsity)
     if tensor_peak:
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(tensor_peak, 1),
                 "unit": unit, "frac": round(achieved / tensor_peak, 4),
+                "frac_spec": round(achieved / spec_peak, 4),
                 "traffic": traffic, "kernel": kname, "kernel_ms": round(main_ms, 4),
                 "peak_source": f"{peak_kind} bf16 dense"
                                + (" x2 (int8 dense rate)" if int8 else "")}
