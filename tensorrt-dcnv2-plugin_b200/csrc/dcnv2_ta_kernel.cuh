@@ -7,8 +7,9 @@
 // there. Per K-block of 128 pixels x 128 bytes this saves the 16 KB shared-memory store of the A
 // tile and the tensor core's 16 KB shared-memory read of it, which leaves shared memory to the
 // corner reads (64 KB) and the weight tiles. TMEM holds the accumulator (256 columns, so at most
-// 256 output channels per tile; wider layers run several output-channel chunks) and a ring of
-// up to 8 A stages (32 columns each).
+// 256 output channels per tile; wider layers run several output-channel chunks), for fp16 a park
+// area of 128 columns (the converted tile, stored to y while the next tile's MMAs run), and a
+// ring of A stages of 32 columns (4 for fp16, 8 for int8).
 //
 // Roles (576 threads; 18 warps leave each thread 96 registers):
 //   warp 0       producer: bulk copy of each K-block's pre-swizzled weight tile (B ring, smem)
@@ -18,9 +19,9 @@
 //   warps 6-17   samplers: warp w fills TMEM lane quadrant w % 4 (32 pixels, thread = pixel),
 //                whole 128-byte rows of the K-blocks of taps t = (w - 6) / 4 (mod 3)
 // The x window is stored linearly (128 bytes per pixel, so 16-byte chunk c of any pixel sits in
-// bank group c). In the 3x3 fp16 fast path lane i reads chunk h ^ (i % 8) at step h: the 8 lanes
-// of each 128-bit load phase hit 8 different bank groups whatever the offsets, and a register
-// butterfly restores the chunk order before the TMEM store.
+// bank group c). In the 3x3 fast path (fp16 and int8) lane i reads chunk h ^ (i % 8) at step h:
+// the 8 lanes of each 128-bit load phase hit 8 different bank groups whatever the offsets, and a
+// register butterfly restores the chunk order before the TMEM store.
 #pragma once
 #include "dcnv2_kernels.cuh"
 
