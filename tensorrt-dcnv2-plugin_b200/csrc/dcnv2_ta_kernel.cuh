@@ -21,7 +21,10 @@
 // The x window is stored linearly (128 bytes per pixel, so 16-byte chunk c of any pixel sits in
 // bank group c). In the 3x3 fast path (fp16 and int8) lane i reads chunk h ^ (i % 8) at step h:
 // the 8 lanes of each 128-bit load phase hit 8 different bank groups whatever the offsets, and a
-// register butterfly restores the chunk order before the TMEM store.
+// register butterfly restores the chunk order before the TMEM store. The x windows are double
+// buffered; the sampler warp that is last to finish with a buffer issues the TMA load of the
+// window two channel blocks ahead into it (a shared-memory count per buffer), so no sampler
+// waits for the others at a channel-block boundary.
 #pragma once
 #include "dcnv2_kernels.cuh"
 
@@ -209,9 +212,12 @@ __global__ void __launch_bounds__(kTaThreads, 1)
   const uint32_t tempty = tfull + 8;              // accumulator read by the epilogue(s)
   const uint32_t drain = tempty + 8;
   const uint32_t win_full = drain + 8;            // [2]
-  const uint32_t win_empty = win_full + 16;       // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * SA + 2 * SB + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // [2] sampler warps done with window buffer b, counted over the kernel (the warp that
+  // completes a use loads the buffer's next window), and the number of windows issued
+  uint32_t* win_done = tmem_slot + 2;
+  uint32_t* win_issued = tmem_slot + 4;
   // bias of the (single) output-channel chunk as fp32, after the 512 bytes of barriers
   float* bias_smem = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 512);
   const WaitCtx wc{args.timeout_ns, args.err, abort_flag};
@@ -235,8 +241,9 @@ __global__ void __launch_bounds__(kTaThreads, 1)
     ptx::mbar_init(drain, 1);
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(win_full + 8 * i, 1);
-      ptx::mbar_init(win_empty + 8 * i, kTaSampWarps);
+      win_done[i] = 0;
     }
+    *win_issued = 0;
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -528,31 +535,30 @@ __global__ void __launch_bounds__(kTaThreads, 1)
     const int K = KT == 9 ? 3 : args.K;
     int kb_seq = 0;    // K-blocks of this CTA before the current channel block
     int cbi = 0;       // channel-block sequence number (window buffer cbi & 1)
-    int issued = 0;    // windows issued (issuer)
     bool ok = true;
     bool pending = false;  // a TMEM store of stage pend_s not yet published
     int pend_s = 0;
 
-    auto issue_window = [&](int qq) -> bool {
+    // Loads window qq (the CTA's channel-block sequence number) into buffer qq & 1, which no
+    // warp reads any more. One thread.
+    auto issue_window = [&](int qq) {
       const int k = qq / cb_per_tile, r = qq - k * cb_per_tile;
       const int tl = tile0 + k * tstep;
-      if (tl >= args.num_tiles) return true;
+      if (tl >= args.num_tiles) return;
       const int g = r / args.CBg, cbg = r - g * args.CBg;
       int im, pt, cc;
       decode_tile(args, tl, im, pt, cc);
       const int row0 = (pix_base(pt) / args.Wo) * args.stride - args.win_top;
       const int b = qq & 1;
-      const uint32_t use = static_cast<uint32_t>(qq >> 1) & 1u;
-      if (!wait_bar<kSuspend>(win_empty + 8 * b, use ^ 1u, wc, DCNV2_DEVERR_TIMEOUT_SAMPLER))
-        return false;
       ptx::mbar_arrive_expect_tx(win_full + 8 * b, args.win_bytes);
       ptx::tma_load_4d(w_base + b * args.win_stride, &tmap_x, (g * args.Cg + cbg * KC) * EB, 0,
                        row0, im, win_full + 8 * b);
-      issued = qq + 1;
-      return true;
+      atomicMax(win_issued, static_cast<uint32_t>(qq + 1));
     };
-    if (issuer) ok = issue_window(0) && issue_window(1);
-    ok = __all_sync(0xffffffffu, ok);
+    if (issuer) {
+      issue_window(0);
+      issue_window(1);
+    }
 
     auto prefetch_geometry = [&](int tl) {
       if (tl >= args.num_tiles) return;
@@ -785,14 +791,19 @@ __global__ void __launch_bounds__(kTaThreads, 1)
           }
           if (!ok) break;
           if (args.use_win) {
-            // every corner load of this channel block has returned (its values are mixed)
+            // every corner load of this channel block has returned (its values are mixed); the
+            // last warp to finish with the buffer loads the window two channel blocks ahead
+            // into it, so no warp waits for the others here
             __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(win_empty + 8 * b);
-            // the issuer may wait below for the other warps: publish this warp's last stage first
-            if (sw == 0) flush();
-            bool iok = true;
-            if (issuer) iok = issue_window(cbi + 2);
-            if (!__all_sync(0xffffffffu, iok)) { ok = false; break; }
+            if (lane == 0) {
+              __threadfence_block();
+              const uint32_t uses = static_cast<uint32_t>(cbi >> 1) + 1u;
+              if (atomicAdd(win_done + b, 1u) == uses * kTaSampWarps - 1u) {
+                __threadfence_block();
+                ptx::fence_proxy_async_smem();
+                issue_window(cbi + 2);
+              }
+            }
           }
           ++cbi;
           kb_seq += T;
@@ -801,16 +812,18 @@ __global__ void __launch_bounds__(kTaThreads, 1)
     }
     if (ok) flush();
     else if (pending) ptx::tmem_wait_st();
-    if (issuer) {
-      for (int qq = issued - 2 < 0 ? 0 : issued - 2; qq < issued; ++qq)
-        wait_bar(win_full + 8 * (qq & 1), static_cast<uint32_t>(qq >> 1) & 1u, wc,
-                 DCNV2_DEVERR_TIMEOUT_DRAIN);
-    }
   }
 
   ptx::tc_fence_before();
   if (PAIR) ptx::cluster_sync();
   else __syncthreads();
+  if (args.use_win && warp == kSampWarp0 && lane == 0) {
+    // window loads still in flight (after an early exit) land before shared memory is released
+    const int issued = static_cast<int>(*reinterpret_cast<volatile uint32_t*>(win_issued));
+    for (int qq = issued - 2 < 0 ? 0 : issued - 2; qq < issued; ++qq)
+      wait_bar(win_full + 8 * (qq & 1), static_cast<uint32_t>(qq >> 1) & 1u, wc,
+               DCNV2_DEVERR_TIMEOUT_DRAIN);
+  }
   if (warp == kMmaWarp) {
     __syncwarp();
     ptx::tc_fence_after();
