@@ -105,13 +105,14 @@ DCNV2_API dcnv2_status dcnv2_forward(const dcnv2_desc* desc,
 
 /* ---- Host-buffer forward (copies overlapped with compute) ---- */
 
-/* Workspace bytes for dcnv2_forward_host with chunks of `images_per_chunk` images (0 picks the
- * chunk: about an eighth of the batch). Returns 0 on a bad desc. */
+/* Workspace bytes for dcnv2_forward_host with chunks of at most `images_per_chunk` images (0
+ * picks the chunk: about an eighth of the batch). Returns 0 on a bad desc. */
 DCNV2_API size_t dcnv2_forward_host_workspace_size(const dcnv2_desc* desc,
                                                    int32_t images_per_chunk);
 
 /* dcnv2_forward with x, offset, mask and y in HOST memory (weight and bias stay device pointers,
- * as the plugin's constants are). The batch runs in chunks of images: the upload of chunk i+1,
+ * as the plugin's constants are). The batch runs in chunks of images (the first and the last a
+ * quarter of the others, when the batch spans more than two): the upload of chunk i+1,
  * the forward of chunk i and the download of chunk i-1 overlap on two library-owned copy streams
  * (created once per device) and `stream`, ordered by events. Asynchronous like cudaMemcpyAsync:
  * y is complete when `stream` has completed. Host buffers must be page-locked for the copies to

@@ -871,6 +871,11 @@ CopyStreams* copy_streams(int dev) {
   return g_copy_streams[dev].ok ? &g_copy_streams[dev] : nullptr;
 }
 
+// Slots of the host-buffer forward: each holds x, offset, mask and y of one chunk, so that the
+// upload of a chunk, the forward of the one before and the downloads of earlier ones overlap.
+// Three or four slots measured the same as two (the bus, not the slot ring, sets the pace).
+constexpr int kHostSlots = 2;
+
 struct HostChunking {
   int chunk = 0;                        // images per chunk
   size_t x_img = 0, off_img = 0, mask_img = 0, y_img = 0;  // bytes per image
@@ -905,7 +910,7 @@ dcnv2_status host_chunking(const dcnv2_desc* desc, int32_t ipc, HostChunking* hc
   hc->mask_off = off; off = dcnv2::align_up(off + chunk * hc->mask_img, 256);
   hc->y_off = off;    off = dcnv2::align_up(off + chunk * hc->y_img, 256);
   hc->slot_bytes = off;
-  hc->fwd_off = 2 * off;
+  hc->fwd_off = kHostSlots * off;
   hc->fwd_bytes = p.ws_bytes;
   hc->total = hc->fwd_off + p.ws_bytes + 256;
   return DCNV2_OK;
@@ -938,14 +943,15 @@ extern "C" dcnv2_status dcnv2_forward_host(const dcnv2_desc* desc, const void* x
       dcnv2::align_up(reinterpret_cast<uintptr_t>(workspace), 256));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // events: entry, and per slot: inputs landed, forward done, output landed
-  cudaEvent_t ev[7] = {};
+  cudaEvent_t ev[1 + 3 * kHostSlots] = {};
   for (auto& e : ev)
     if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
       for (auto& f : ev) if (f) cudaEventDestroy(f);
       cudaGetLastError();
       return DCNV2_ERR_CUDA;
     }
-  cudaEvent_t ev_entry = ev[0], *ev_in = ev + 1, *ev_fwd = ev + 3, *ev_out = ev + 5;
+  cudaEvent_t ev_entry = ev[0], *ev_in = ev + 1, *ev_fwd = ev_in + kHostSlots,
+              *ev_out = ev_fwd + kHostSlots;
   const int N = desc->n;
   const uint8_t* xh = static_cast<const uint8_t*>(x_host);
   const uint8_t* oh = static_cast<const uint8_t*>(offset_host);
@@ -954,13 +960,24 @@ extern "C" dcnv2_status dcnv2_forward_host(const dcnv2_desc* desc, const void* x
   bool ok = cudaEventRecord(ev_entry, st) == cudaSuccess &&  // earlier work on `stream` first
             cudaStreamWaitEvent(cs->h2d, ev_entry, 0) == cudaSuccess &&
             cudaStreamWaitEvent(cs->d2h, ev_entry, 0) == cudaSuccess;
+  // Chunk sizes: the first and the last chunk hold a quarter of the others' images (when the
+  // batch spans more than two chunks). The upload before the first forward and the download
+  // after the last one overlap nothing, so they are kept short; in between, uploads and
+  // downloads share the bus in both directions.
+  const int edge = hc.chunk >= 4 && N > 2 * hc.chunk ? hc.chunk / 4 : hc.chunk;
+  auto chunk_at = [&](int n0) {
+    const int left = N - n0;
+    if (n0 == 0 || left <= edge) return left < edge ? left : edge;
+    if (left - hc.chunk < edge) return left - edge;  // leaves `edge` images for the last chunk
+    return hc.chunk;
+  };
   int i = 0;
-  for (int n0 = 0; ok && n0 < N; n0 += hc.chunk, ++i) {
-    const int nb = N - n0 < hc.chunk ? N - n0 : hc.chunk;
-    const int b = i & 1;
+  for (int n0 = 0, nb = 0; ok && n0 < N; n0 += nb, ++i) {
+    nb = chunk_at(n0);
+    const int b = i % kHostSlots;
     uint8_t* slot = ws + b * hc.slot_bytes;
-    // upload (slot b is free once the forward of chunk i-2 has read it)
-    if (i >= 2) ok = ok && cudaStreamWaitEvent(cs->h2d, ev_fwd[b], 0) == cudaSuccess;
+    // upload (slot b is free once the forward of chunk i - kHostSlots has read it)
+    if (i >= kHostSlots) ok = ok && cudaStreamWaitEvent(cs->h2d, ev_fwd[b], 0) == cudaSuccess;
     ok = ok &&
          cudaMemcpyAsync(slot + hc.x_off, xh + n0 * hc.x_img, nb * hc.x_img,
                          cudaMemcpyHostToDevice, cs->h2d) == cudaSuccess &&
@@ -969,9 +986,9 @@ extern "C" dcnv2_status dcnv2_forward_host(const dcnv2_desc* desc, const void* x
          cudaMemcpyAsync(slot + hc.mask_off, mh + n0 * hc.mask_img, nb * hc.mask_img,
                          cudaMemcpyHostToDevice, cs->h2d) == cudaSuccess &&
          cudaEventRecord(ev_in[b], cs->h2d) == cudaSuccess;
-    // forward (its y slot is free once the download of chunk i-2 has read it)
+    // forward (its y slot is free once the download of chunk i - kHostSlots has read it)
     ok = ok && cudaStreamWaitEvent(st, ev_in[b], 0) == cudaSuccess;
-    if (i >= 2) ok = ok && cudaStreamWaitEvent(st, ev_out[b], 0) == cudaSuccess;
+    if (i >= kHostSlots) ok = ok && cudaStreamWaitEvent(st, ev_out[b], 0) == cudaSuccess;
     if (ok) {
       dcnv2_desc d = *desc;
       d.n = nb;
@@ -986,7 +1003,7 @@ extern "C" dcnv2_status dcnv2_forward_host(const dcnv2_desc* desc, const void* x
          cudaEventRecord(ev_out[b], cs->d2h) == cudaSuccess;
   }
   // `stream` completes after every download
-  for (int b = 0; ok && b < 2 && b < i; ++b)
+  for (int b = 0; ok && b < kHostSlots && b < i; ++b)
     ok = cudaStreamWaitEvent(st, ev_out[b], 0) == cudaSuccess;
   for (auto& e : ev) cudaEventDestroy(e);  // released once the work that uses them completes
   if (!ok) {

@@ -391,6 +391,22 @@ def test_host_buffer_forward_matches_device_forward(chunk):
     assert torch.equal(y8, ref8.cpu())
 
 
+@pytest.mark.parametrize("chunk", [4, 8])
+def test_host_buffer_forward_short_edge_chunks(chunk):
+    """A batch of more than two chunks runs with a first and a last chunk of a quarter of the
+    others (20 images in chunks of 4: 1, 4, 4, 4, 4, 2, 1; of 8: 2, 8, 8, 2); the result stays
+    bit-identical to dcnv2_forward."""
+    from dcnv2_b200 import dcnv2_forward_host
+    fx = random_case(n=20, c=32, o=32, h=12, w=12, ostd=0.6, outl=0.02, seed=13)
+    host = [torch.from_numpy(fx[k]).to(torch.float16).contiguous().pin_memory()
+            for k in ("x", "offset", "mask")]
+    w = cuda(fx["weight"], torch.float16)
+    b = cuda(fx["bias"], torch.float16)
+    ref = dcnv2_forward(*[h.to(DEV) for h in host], w, b, **attrs(fx))
+    y = dcnv2_forward_host(*host, w, b, images_per_chunk=chunk, **attrs(fx))
+    assert torch.equal(y, ref.cpu())
+
+
 def test_levels_runner_graph_matches_per_level_forward():
     """The FPN levels run as one CUDA graph with one stream per level give the same outputs,
     bit for bit, as one dcnv2_forward per level."""
