@@ -72,7 +72,10 @@ __device__ __noinline__ void ta_mma_issuer(const TaMmaParams mp) {
   uint32_t pa = 0, pb = 0, use = 0;
   bool ok = true;
   for (int tile = mp.tile0; tile < mp.num_tiles && ok; tile += mp.tstep) {
-    if (!wait_bar<64, PAIR>(mp.tempty, use ^ 1u, wc, DCNV2_DEVERR_TIMEOUT_MMA)) {
+    // the accumulator drained: a suspended wait wakes when the phase completes (the CTA pair's
+    // leader polls its cluster-scope barrier)
+    if (!(PAIR ? wait_bar<64, true>(mp.tempty, use ^ 1u, wc, DCNV2_DEVERR_TIMEOUT_MMA)
+               : wait_bar<kSuspend>(mp.tempty, use ^ 1u, wc, DCNV2_DEVERR_TIMEOUT_MMA))) {
       ok = false;
       break;
     }
