@@ -693,12 +693,29 @@ __global__ void __launch_bounds__(kTaThreads, 1)
               const uint32_t w23 = __byte_perm(cw[u][2], cw[u][3], 0x5410);
               // step h: chunk h ^ rot of every corner (conflict-free phases), mixed into out[4h..]
               uint32_t out[32];
+              // int8: the loads of chunk h + 1 are issued before chunk h is mixed (its integer
+              // mix is long enough to cover their latency)
+              uint4 xn[4];
+              if constexpr (PREC == PREC_I8) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) xn[c] = ptx::ld_shared_v4(pix[c] + rot16);
+              }
 #pragma unroll
               for (int h = 0; h < 8; ++h) {
                 const uint32_t co = (static_cast<uint32_t>(h) << 4) ^ rot16;
                 uint4 xv[4];
+                if constexpr (PREC == PREC_I8) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c) xv[c] = ptx::ld_shared_v4(pix[c] + co);
+                  for (int c = 0; c < 4; ++c) xv[c] = xn[c];
+                  if (h + 1 < 8) {
+                    const uint32_t cn = (static_cast<uint32_t>(h + 1) << 4) ^ rot16;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) xn[c] = ptx::ld_shared_v4(pix[c] + cn);
+                  }
+                } else {
+#pragma unroll
+                  for (int c = 0; c < 4; ++c) xv[c] = ptx::ld_shared_v4(pix[c] + co);
+                }
                 // the previous K-block's TMEM store has had time to land: publish it now rather
                 // than after this whole K-block
                 if (h == 0) flush();
