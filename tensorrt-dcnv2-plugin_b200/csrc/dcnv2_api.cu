@@ -628,8 +628,17 @@ dcnv2_status launch_f32_exact(const Plan& p, DevInfo* di, const void* x, const v
   a.K = p.K; a.T = p.T; a.stride = p.stride; a.pad = p.pad; a.dil = p.dil; a.dg = p.dg;
   a.Cg = p.Cg; a.CBg = p.CBg; a.numKB = p.numKB; a.ptiles = p.x_ptiles; a.ctiles = p.x_ctiles;
   const int64_t grid = int64_t(p.N) * p.x_ptiles * p.x_ctiles;
+  constexpr uint32_t kExactBit = 1u << 4;
+  if (!(di->attr_set.load(std::memory_order_acquire) & kExactBit)) {
+    if (cudaFuncSetAttribute(dcnv2_f32_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kXSmemBytes)) != cudaSuccess) {
+      cudaGetLastError();
+      return DCNV2_ERR_CUDA;
+    }
+    di->attr_set.fetch_or(kExactBit, std::memory_order_acq_rel);
+  }
   mk.mark(st);
-  dcnv2_f32_exact_kernel<<<static_cast<unsigned>(grid), kXThreads, 0, st>>>(a);
+  dcnv2_f32_exact_kernel<<<static_cast<unsigned>(grid), kXThreads * kXGroups, kXSmemBytes, st>>>(a);
   mk.mark(st);
   return cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
 }

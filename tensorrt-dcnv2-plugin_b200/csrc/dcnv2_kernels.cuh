@@ -1224,9 +1224,16 @@ __global__ void __launch_bounds__(256) pack_weights_kernel(const void* __restric
 // the ~900 accumulation steps of a 3xTF32 product at C*K*K = 2304 its error reaches ~5e-5
 // relative. This kernel is the fp32-exact path: the same fused structure (samples go straight
 // to shared memory, K ordered (group, tap, 32-channel block), no column matrix in HBM), with the
-// GEMM on CUDA cores in fp32 FMA. CTA tile: 64 output pixels x 128 output channels, 256
-// threads, each accumulating 4 pixels x 8 channels; double-buffered shared-memory stages.
-constexpr int kXPx = 64, kXCo = 128, kXK = 32, kXThreads = 256;
+// GEMM on CUDA cores in fp32 FMA. CTA tile: 64 output pixels x 128 output channels, computed by
+// two groups of 256 threads that split the K-blocks in halves (each thread accumulates 4 pixels x
+// 8 channels of its half; double-buffered shared-memory stages per group); the second group's
+// sums are added to the first's at the end, so every output is (first half) + (second half) +
+// bias whatever the batch. Two groups give 16 warps per SM where one image leaves 128 CTAs for
+// 148 SMs.
+constexpr int kXPx = 64, kXCo = 128, kXK = 32, kXThreads = 256, kXGroups = 2;
+// dynamic shared memory: per group A [2][kXK][kXPx] and B [2][kXK][kXCo] floats
+constexpr int kXGroupFloats = 2 * kXK * kXPx + 2 * kXK * kXCo;
+constexpr size_t kXSmemBytes = size_t(kXGroups) * kXGroupFloats * sizeof(float);
 
 struct ExactArgs {
   const float* x_nhwc;   // [N][H][W][C]
@@ -1239,10 +1246,17 @@ struct ExactArgs {
   int ptiles, ctiles;
 };
 
-__global__ void __launch_bounds__(kXThreads, 2) dcnv2_f32_exact_kernel(const ExactArgs a) {
-  __shared__ __align__(16) float As[2][kXK][kXPx];
-  __shared__ __align__(16) float Bs[2][kXK][kXCo];
-  const int tid = threadIdx.x;
+__global__ void __launch_bounds__(kXThreads * kXGroups, 1) dcnv2_f32_exact_kernel(const ExactArgs a) {
+  extern __shared__ __align__(16) float xsm[];
+  const int grp = threadIdx.x / kXThreads;  // K half
+  const int tid = threadIdx.x - grp * kXThreads;
+  float (*As)[kXK][kXPx] = reinterpret_cast<float (*)[kXK][kXPx]>(xsm + grp * kXGroupFloats);
+  float (*Bs)[kXK][kXCo] =
+      reinterpret_cast<float (*)[kXK][kXCo]>(xsm + grp * kXGroupFloats + 2 * kXK * kXPx);
+  const int half = (a.numKB + 1) / 2;
+  const int kb_begin = grp == 0 ? 0 : half, kb_end = grp == 0 ? half : a.numKB;
+  // the two groups synchronise separately (their K ranges may differ in length)
+  auto group_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(kXThreads)); };
   const int ct = blockIdx.x % a.ctiles;
   const int pt = (blockIdx.x / a.ctiles) % a.ptiles;
   const int img = blockIdx.x / (a.ctiles * a.ptiles);
@@ -1275,7 +1289,7 @@ __global__ void __launch_bounds__(kXThreads, 2) dcnv2_f32_exact_kernel(const Exa
     const int cbg = kb % a.CBg;
     const int t = (kb / a.CBg) % a.T;
     const int g = kb / (a.CBg * a.T);
-    if (cbg == 0) {  // new (group, tap): new sampling geometry
+    if (cbg == 0 || kb == kb_begin) {  // new (group, tap): new sampling geometry
       const int ki = t / a.K, kj = t - ki * a.K;
       float dh = 0.f, dw = 0.f, m = 0.f;
       if (pvalid) {
@@ -1325,12 +1339,14 @@ __global__ void __launch_bounds__(kXThreads, 2) dcnv2_f32_exact_kernel(const Exa
     for (int i = 0; i < 4; ++i) bd[tid + i * kXThreads] = bq[i];
   };
 
-  prefetch(0);
-  store(0);
-  __syncthreads();
-  for (int kb = 0; kb < a.numKB; ++kb) {
-    const int buf = kb & 1;
-    const bool more = kb + 1 < a.numKB;
+  if (kb_begin < kb_end) {
+    prefetch(kb_begin);
+    store(0);
+  }
+  group_sync();
+  for (int kb = kb_begin; kb < kb_end; ++kb) {
+    const int buf = (kb - kb_begin) & 1;
+    const bool more = kb + 1 < kb_end;
     if (more) prefetch(kb + 1);
 #pragma unroll 8
     for (int k = 0; k < kXK; ++k) {
@@ -1345,8 +1361,22 @@ __global__ void __launch_bounds__(kXThreads, 2) dcnv2_f32_exact_kernel(const Exa
         for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(ar[i], br[j], acc[i][j]);
     }
     if (more) store(buf ^ 1);
-    __syncthreads();
+    group_sync();
   }
+  // the second half's sums, through shared memory ([32 values][256 threads]: conflict-free)
+  float* red = xsm + kXGroupFloats;
+  if (grp == 1) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) red[(i * 8 + j) * kXThreads + tid] = acc[i][j];
+  }
+  __syncthreads();
+  if (grp == 1) return;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = __fadd_rn(acc[i][j], red[(i * 8 + j) * kXThreads + tid]);
   float* yimg = a.y + static_cast<size_t>(img) * a.O * a.P;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
