@@ -324,6 +324,8 @@ def test_cta_pair_and_single_cta_paths_agree(shape, monkeypatch):
 TA_SHAPES = {
     # identity-like offsets: every corner in the x window (fp16 3x3 fast path)
     "c256_o256_hw64_idlike": dict(n=2, c=256, o=256, h=64, w=64, ostd=0.1),
+    # more tiles than SMs: CTAs take two tiles, window buffers are reused across tiles
+    "c128_o64_n10_multitile": dict(n=10, c=128, o=64, h=48, w=48, ostd=0.3),
     # out-of-image offsets: corners outside the window come from global memory
     "c256_o256_oob": dict(n=1, c=256, o=256, h=32, w=48, ostd=0.5, outl=0.05),
     # partial channel block (16 of 64 / 128 channels), 5x5 taps
