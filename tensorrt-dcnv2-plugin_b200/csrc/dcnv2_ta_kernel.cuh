@@ -319,21 +319,23 @@ __global__ void __launch_bounds__(kTaThreads, 1)
       mp.tstep = tstep; mp.numKB = args.numKB; mp.n_mma = args.n_mma;
       mp.wc = wc;
       ta_mma_issuer<PREC, PAIR>(mp);
-    } else if (PAIR && lane == 0) {
+    } else if (PAIR && rank != 0) {
       // Rank 1 relay: once this CTA's A stage (TMEM) and B stage (smem) of a K-block are
-      // complete, tell the leader.
+      // complete, tell the leader. The whole warp runs the loop (lane 0 arrives), so no lane of
+      // it waits at the kernel's final barrier meanwhile.
       const uint32_t peer = ptx::mapa_shared(peer_full, 0);
       int sa = 0, sb = 0;
       uint32_t pa = 0, pb = 0;
       bool ok = true;
       for (int tile = tile0; tile < args.num_tiles && ok; tile += tstep) {
         for (int kb = 0; kb < args.numKB; ++kb) {
-          if (!wait_bar(a_full + 8 * sa, pa, wc, DCNV2_DEVERR_TIMEOUT_MMA) ||
-              !wait_bar(b_full + 8 * sb, pb, wc, DCNV2_DEVERR_TIMEOUT_MMA)) {
+          const bool got = wait_bar<kSuspend>(a_full + 8 * sa, pa, wc, DCNV2_DEVERR_TIMEOUT_MMA) &&
+                           wait_bar<kSuspend>(b_full + 8 * sb, pb, wc, DCNV2_DEVERR_TIMEOUT_MMA);
+          if (!__all_sync(0xffffffffu, got)) {
             ok = false;
             break;
           }
-          ptx::mbar_arrive_cluster(peer + 8 * sa);
+          if (lane == 0) ptx::mbar_arrive_cluster(peer + 8 * sa);
           if (++sa == SA) { sa = 0; pa ^= 1u; }
           if (++sb == SB) { sb = 0; pb ^= 1u; }
         }
