@@ -7,7 +7,8 @@
  * types and raw device pointers only, so any FFI (ctypes, cgo, JNI, a TensorRT IPluginV3 shim)
  * can bind them. All functions are thread-safe and reentrant; the library holds no global
  * handles apart from per-device launch attributes and, for dcnv2_forward_host, two copy streams
- * per device, each set up once.
+ * per device, each set up once. Kernel-selection overrides for measurements (dcnv2_diag.h) are
+ * read from the environment once per process; the dispatch never calls getenv.
  *
  * Tensor contract (src/dcn_plugin.cpp:76,134; python/01_oracle_and_export.py:73-75):
  *   input 0  x       [N, C, H, W]                 linear NCHW
@@ -153,6 +154,13 @@ DCNV2_API dcnv2_status dcnv2_forward_static_scratch(const dcnv2_desc* desc, cons
                                                    const void* weight, const void* bias, void* y,
                                                    float x_scale, float w_scale,
                                                    dcnv2_stream_t stream);
+
+/* Copies the device error word of the last dcnv2_forward_static_scratch call on the current device
+ * (which lives in the static buffer, an address the caller never sees) to *code, after
+ * synchronising `stream`: 0 = none, otherwise DCNV2_DEVERR_* bits, with DCNV2_ERR_DEVICE_TIMEOUT
+ * returned. The word belongs to whichever call ran last on the device. Allocates nothing. No
+ * counterpart in the reference plugin (it reports no device-side errors). */
+DCNV2_API dcnv2_status dcnv2_read_static_scratch_error(dcnv2_stream_t stream, int32_t* code);
 
 /* Copies the device error word of the last forward that used `workspace` to *code (0 = none;
  * otherwise DCNV2_DEVERR_* bits) after synchronising `stream`. Test and debug helper. */

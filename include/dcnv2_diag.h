@@ -37,6 +37,20 @@ DCNV2_API dcnv2_status dcnv2_diag_forward_events(const dcnv2_desc* desc, const v
  * measurements and matching profiler output. */
 DCNV2_API const char* dcnv2_diag_main_kernel(const dcnv2_desc* desc);
 
+/* Kernel selection for measurements and tests, process-wide. kernel: 0 = automatic (A operand in
+ * tensor memory for fp16 / int8 layers of at most 256 output channels, in shared memory above),
+ * 1 = A in tensor memory for every fp16 / int8 layer (one output-channel chunk of at most 256 per
+ * tile), 2 = A in shared memory always. pair: 1 = fp16 / int8 tiles run on CTA pairs
+ * (tcgen05 cta_group::2), 0 = one CTA per tile (the default). The starting values come from the
+ * environment, read once per process: DCNV2_KERNEL=ta|smem, DCNV2_PAIR=1. Change the selection
+ * only between forwards: dcnv2_workspace_size and dcnv2_forward must see the same one. */
+DCNV2_API dcnv2_status dcnv2_diag_set_kernel_override(int32_t kernel, int32_t pair);
+
+/* Architecture of the device code this library runs on the current device, as the runtime
+ * reports it for the main fp16 kernel (cudaFuncAttributes::binaryVersion: 100 = sm_100).
+ * Returns DCNV2_ERR_NO_DEVICE when the device cannot run the library's code. */
+DCNV2_API dcnv2_status dcnv2_diag_binary_arch(int32_t* binary_version);
+
 #ifdef __cplusplus
 }
 #endif

@@ -266,8 +266,24 @@ typedef struct {
   const oracle_shape* s;
   int Ho, Wo, T;
   const int8_t* x; const float* off; const float* mask;
-  int8_t* cq; /* [C*T][P] */
+  int8_t* cq; /* [C*T][np] for output pixels [p0, p0 + np) */
+  int p0, np;
+  int rule;   /* 0: fixed-point rule of the kernels; 1: clamp(rint(m * bilinear(x_q))) */
 } qcols_ctx;
+
+/* src/dcn_kernel.cu:19-30 on an int8 plane: ref_bilinear with each corner value widened to
+ * float as the reference's int8 im2col reads it (:218-235). */
+static float ref_bilinear_i8(const int8_t* in, int H, int W, float h, float w) {
+  if (h <= -1.f || h >= (float)H || w <= -1.f || w >= (float)W) return 0.f;
+  int h_low = (int)floorf(h), w_low = (int)floorf(w);
+  int h_high = h_low + 1, w_high = w_low + 1;
+  float lh = h - (float)h_low, lw = w - (float)w_low, hh = 1.f - lh, hw = 1.f - lw;
+  float v1 = (h_low >= 0 && w_low >= 0) ? (float)in[h_low * W + w_low] : 0.f;
+  float v2 = (h_low >= 0 && w_high <= W - 1) ? (float)in[h_low * W + w_high] : 0.f;
+  float v3 = (h_high <= H - 1 && w_low >= 0) ? (float)in[h_high * W + w_low] : 0.f;
+  float v4 = (h_high <= H - 1 && w_high <= W - 1) ? (float)in[h_high * W + w_high] : 0.f;
+  return hh * hw * v1 + hh * lw * v2 + lh * hw * v3 + lh * lw * v4;
+}
 
 static float i8_mask(float m) { return isnan(m) ? 0.f : fminf(fmaxf(m, 0.f), 1.f); }
 /* 16-bit fixed-point corner weight: rint(a * 2^16) (nearest even), 0 for NaN or a <= 0,
@@ -298,15 +314,23 @@ static void qcols_range(void* vctx, int64_t b, int64_t e) {
     const float* dhp = q->off + ((size_t)(g * 2 * T + 2 * t)) * P;
     const float* dwp = q->off + ((size_t)(g * 2 * T + 2 * t + 1)) * P;
     const float* mp = q->mask + ((size_t)(g * T + t)) * P;
-    int8_t* out = q->cq + (size_t)ct * P;
-    for (int oh = 0; oh < q->Ho; ++oh)
-      for (int ow = 0; ow < q->Wo; ++ow) {
-        int p = oh * q->Wo + ow;
-        tap_geom gm = kernel_geom(H, W, oh * s->stride - s->padding + i * s->dilation,
-                                  ow * s->stride - s->padding + j * s->dilation, dhp[p], dwp[p],
-                                  i8_mask(mp[p]));
-        out[p] = requant(&gm, plane);
+    int8_t* out = q->cq + (size_t)ct * q->np;
+    for (int pi = 0; pi < q->np; ++pi) {
+      const int p = q->p0 + pi, oh = p / q->Wo, ow = p % q->Wo;
+      const int bh = oh * s->stride - s->padding + i * s->dilation;
+      const int bw = ow * s->stride - s->padding + j * s->dilation;
+      if (q->rule == 0) {
+        tap_geom gm = kernel_geom(H, W, bh, bw, dhp[p], dwp[p], i8_mask(mp[p]));
+        out[pi] = requant(&gm, plane);
+      } else {
+        /* the reference's fp32 column (dcn_kernel.cu:218-235) rounded to nearest (even) */
+        const float v = mp[p] * ref_bilinear_i8(plane, H, W, (float)bh + dhp[p],
+                                                (float)bw + dwp[p]);
+        float r = rintf(v);
+        r = r < -127.f ? -127.f : (r > 127.f ? 127.f : r);
+        out[pi] = (int8_t)(isnan(v) ? 0.f : r);
       }
+    }
   }
 }
 
@@ -330,42 +354,60 @@ static void igemm_range(void* vctx, int64_t b, int64_t e) {
 }
 
 /*
- * Exact INT8: cq per column value by the fixed-point rule of requant() above,
+ * Exact INT8 on output pixels [p_begin, p_end) of every image: cq per column value by
+ * `rule` (0: the fixed-point rule of requant() above, which the kernels implement; 1: the
+ * reference's fp32 column m * bilinear(x_q) rounded to nearest and clamped to [-127, 127]),
  * acc = sum w_q*cq in int64, y = acc*s + b in double with s = fl32(x_scale*w_scale).
- * acc_out (optional, int64 [N][O][P]) and cols_out (optional, int8 [N][C*T][P]) expose the
- * integer intermediates so that tests can compare them bit for bit.
+ * y, acc_out (optional, int64) and cols_out (optional, int8 [N][C*T][np]) are laid out
+ * [N][O][np] / [N][C*T][np] with np = p_end - p_begin.
  */
-int oracle_forward_i8_exact(const oracle_shape* s, const int8_t* xq, const float* off,
-                            const float* mask, const int8_t* wq, const float* b, float x_scale,
-                            float w_scale, double* y, int64_t* acc_out, int8_t* cols_out,
-                            int threads) {
+int oracle_forward_i8_exact_band(const oracle_shape* s, const int8_t* xq, const float* off,
+                                 const float* mask, const int8_t* wq, const float* b,
+                                 float x_scale, float w_scale, double* y, int64_t* acc_out,
+                                 int8_t* cols_out, int threads, int p_begin, int p_end, int rule) {
   if (!s || s->n <= 0 || s->c <= 0 || s->groups <= 0 || s->c % s->groups) return -1;
+  if (rule != 0 && rule != 1) return -1;
   const int Ho = out_dim(s->h, s->kernel, s->stride, s->padding, s->dilation);
   const int Wo = out_dim(s->w, s->kernel, s->stride, s->padding, s->dilation);
   if (Ho <= 0 || Wo <= 0) return -1;
   const int T = s->kernel * s->kernel, P = Ho * Wo, CKK = s->c * T, O = s->out_c;
+  if (p_begin < 0 || p_end > P || p_begin >= p_end) return -1;
+  const int NP = p_end - p_begin;
   const size_t xi = (size_t)s->c * s->h * s->w;
-  int8_t* cq = (int8_t*)malloc((size_t)CKK * P);
-  int64_t* acc = (int64_t*)malloc(sizeof(int64_t) * (size_t)O * P);
+  int8_t* cq = (int8_t*)malloc((size_t)CKK * NP);
+  int64_t* acc = (int64_t*)malloc(sizeof(int64_t) * (size_t)O * NP);
   if (!cq || !acc) { free(cq); free(acc); return -1; }
   const double scale = (double)(x_scale * w_scale);
   for (int n = 0; n < s->n; ++n) {
     qcols_ctx qc = {s, Ho, Wo, T, xq + (size_t)n * xi, off + (size_t)n * s->groups * 2 * T * P,
-                    mask + (size_t)n * s->groups * T * P, cq};
+                    mask + (size_t)n * s->groups * T * P, cq, p_begin, NP, rule};
     parallel_for(CKK, threads, qcols_range, &qc);
-    if (cols_out) memcpy(cols_out + (size_t)n * CKK * P, cq, (size_t)CKK * P);
-    igemm_ctx gc = {wq, cq, acc, CKK, P};
+    if (cols_out) memcpy(cols_out + (size_t)n * CKK * NP, cq, (size_t)CKK * NP);
+    igemm_ctx gc = {wq, cq, acc, CKK, NP};
     parallel_for(O, threads, igemm_range, &gc);
     for (int o = 0; o < O; ++o)
-      for (int p = 0; p < P; ++p) {
-        int64_t a = acc[(size_t)o * P + p];
-        if (acc_out) acc_out[((size_t)n * O + o) * P + p] = a;
-        if (y) y[((size_t)n * O + o) * P + p] = (double)a * scale + (b ? (double)b[o] : 0.0);
+      for (int p = 0; p < NP; ++p) {
+        int64_t a = acc[(size_t)o * NP + p];
+        if (acc_out) acc_out[((size_t)n * O + o) * NP + p] = a;
+        if (y) y[((size_t)n * O + o) * NP + p] = (double)a * scale + (b ? (double)b[o] : 0.0);
       }
   }
   free(cq);
   free(acc);
   return 0;
+}
+
+/* Whole-image form of oracle_forward_i8_exact_band with the kernels' fixed-point rule. */
+int oracle_forward_i8_exact(const oracle_shape* s, const int8_t* xq, const float* off,
+                            const float* mask, const int8_t* wq, const float* b, float x_scale,
+                            float w_scale, double* y, int64_t* acc_out, int8_t* cols_out,
+                            int threads) {
+  if (!s) return -1;
+  const int Ho = out_dim(s->h, s->kernel, s->stride, s->padding, s->dilation);
+  const int Wo = out_dim(s->w, s->kernel, s->stride, s->padding, s->dilation);
+  if (Ho <= 0 || Wo <= 0) return -1;
+  return oracle_forward_i8_exact_band(s, xq, off, mask, wq, b, x_scale, w_scale, y, acc_out,
+                                      cols_out, threads, 0, Ho * Wo, 0);
 }
 
 /*

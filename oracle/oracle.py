@@ -54,6 +54,11 @@ def lib() -> ctypes.CDLL:
                                               ctypes.c_float, ctypes.POINTER(ctypes.c_double),
                                               ctypes.POINTER(ctypes.c_int64), i8p, ctypes.c_int]
         L.oracle_forward_i8_exact.restype = ctypes.c_int
+        L.oracle_forward_i8_exact_band.argtypes = [
+            Sp, i8p, fp, fp, i8p, fp, ctypes.c_float, ctypes.c_float,
+            ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64), i8p, ctypes.c_int,
+            ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.oracle_forward_i8_exact_band.restype = ctypes.c_int
         L.oracle_quantize_sym.argtypes = [fp, ctypes.c_int64, i8p]
         L.oracle_quantize_sym.restype = ctypes.c_float
         L.oracle_forward_direct.argtypes = [Sp, fp, fp, fp, fp, fp, fp]
@@ -156,6 +161,34 @@ def forward_i8_exact(xq, offset, mask, wq, bias, x_scale, w_scale, stride=1, pad
         threads or os.cpu_count() or 1)
     if rc:
         raise ValueError("oracle_forward_i8_exact failed")
+    return (y, acc, cols) if want_cols else (y, acc)
+
+
+I8_RULES = {"fixed": 0, "rint": 1}
+
+
+def forward_i8_exact_band(xq, offset, mask, wq, bias, x_scale, w_scale, p_begin, p_end,
+                          stride=1, padding=1, dilation=1, groups=1, rule="fixed",
+                          want_cols=False, threads=None):
+    """Exact INT8 on output pixels [p_begin, p_end) of every image. rule "fixed": the column
+    rule the kernels implement (16-bit fixed-point corner weights); rule "rint": the reference's
+    fp32 column m*bilinear(x_q) (src/dcn_kernel.cu:218-235) rounded to nearest, clamped to
+    +-127. Returns (y float64 [N,O,np], acc int64 [N,O,np][, cols int8 [N,C*K*K,np]])."""
+    xq, wq, offset, mask = _i8(xq), _i8(wq), _f32(offset), _f32(mask)
+    b = _f32(bias) if bias is not None else None
+    s = _shape(xq, wq, stride, padding, dilation, groups)
+    npx = int(p_end) - int(p_begin)
+    y = np.empty((s.n, s.out_c, npx), np.float64)
+    acc = np.empty((s.n, s.out_c, npx), np.int64)
+    cols = np.empty((s.n, s.c * s.kernel ** 2, npx), np.int8) if want_cols else None
+    fp, i8 = ctypes.c_float, ctypes.c_int8
+    rc = lib().oracle_forward_i8_exact_band(
+        ctypes.byref(s), _p(xq, i8), _p(offset, fp), _p(mask, fp), _p(wq, i8),
+        _p(b, fp) if b is not None else None, float(x_scale), float(w_scale),
+        _p(y, ctypes.c_double), _p(acc, ctypes.c_int64), _p(cols, i8) if want_cols else None,
+        threads or os.cpu_count() or 1, int(p_begin), int(p_end), I8_RULES[rule])
+    if rc:
+        raise ValueError("oracle_forward_i8_exact_band failed")
     return (y, acc, cols) if want_cols else (y, acc)
 
 

@@ -9,10 +9,28 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "dcn_kernel.h"
 
 namespace {
 int out_dim(int in, int k, int s, int p, int d) { return (in + 2 * p - d * (k - 1) - 1) / s + 1; }
+
+// One cuBLAS handle per device, created on the first call and kept for the process, as the
+// reference plugin creates its handle once, lazily, on its first enqueue
+// (src/dcn_plugin.cpp:131) and keeps it until the plugin is destroyed.
+constexpr int kMaxDev = 64;
+cublasHandle_t g_handle[kMaxDev] = {};
+std::mutex g_handle_mu;
+
+cublasHandle_t handle_for_current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return nullptr;
+  std::lock_guard<std::mutex> lock(g_handle_mu);
+  if (!g_handle[dev] && cublasCreate(&g_handle[dev]) != CUBLAS_STATUS_SUCCESS)
+    g_handle[dev] = nullptr;
+  return g_handle[dev];
+}
 }  // namespace
 
 extern "C" {
@@ -32,9 +50,8 @@ int ref_enqueue(int dtype, int N, int Cin, int H, int W, int Cout, int K, int st
   const int Ho = out_dim(H, K, stride, pad, dil), Wo = out_dim(W, K, stride, pad, dil);
   const int CKK = Cin * K * K, HW = Ho * Wo;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cublasHandle_t h = nullptr;
-  if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) return 1;
-  cublasSetStream(h, st);
+  cublasHandle_t h = handle_for_current_device();
+  if (!h || cublasSetStream(h, st) != CUBLAS_STATUS_SUCCESS) return 1;
   const float one = 1.f, zero = 0.f;
   int rc = 0;
   for (int n = 0; n < N && rc == 0; ++n) {
@@ -82,9 +99,7 @@ int ref_enqueue(int dtype, int N, int Cin, int H, int W, int Cout, int K, int st
     }
     if (cudaGetLastError() != cudaSuccess) rc = 2;
   }
-  // The handle is destroyed after the stream drains so the caller may time the whole call.
-  cudaStreamSynchronize(st);
-  cublasDestroy(h);
+  // Asynchronous like the reference enqueue: nothing waits for the stream here.
   return rc;
 }
 

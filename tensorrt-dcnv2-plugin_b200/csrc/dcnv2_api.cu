@@ -59,6 +59,23 @@ DevInfo* device_info(int dev) {
 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Kernel-selection overrides for measurements and tests. They are read from the environment
+// once per process (DCNV2_KERNEL=ta|smem, DCNV2_PAIR=1) and can be changed afterwards only
+// through dcnv2_diag_set_kernel_override; the dispatch itself never calls getenv.
+enum { KOV_AUTO = 0, KOV_TA = 1, KOV_SMEM = 2 };
+std::atomic<int> g_kernel_override{KOV_AUTO};
+std::atomic<int> g_pair_override{0};
+std::once_flag g_env_once;
+void read_env_overrides() {
+  std::call_once(g_env_once, []() {
+    const char* ke = std::getenv("DCNV2_KERNEL");
+    if (ke && std::strcmp(ke, "smem") == 0) g_kernel_override.store(KOV_SMEM);
+    else if (ke && std::strcmp(ke, "ta") == 0) g_kernel_override.store(KOV_TA);
+    const char* pe = std::getenv("DCNV2_PAIR");
+    g_pair_override.store(pe && pe[0] == '1' && pe[1] == 0 ? 1 : 0);
+  });
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link needed).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -210,6 +227,7 @@ void plan_ta(Plan* pl) {
 
 dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
   if (!d || !pl) return DCNV2_ERR_INVALID_ARG;
+  read_env_overrides();
   if (d->n < 1 || d->c < 1 || d->h < 1 || d->w < 1 || d->out_c < 1 || d->kernel < 1 ||
       d->stride < 1 || d->padding < 0 || d->dilation < 1 || d->deformable_groups < 1)
     return DCNV2_ERR_INVALID_ARG;
@@ -278,10 +296,9 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
     while (cols < static_cast<uint32_t>(p.acc_bufs * p.nrows)) cols <<= 1;
     p.tmem_cols = cols;
     // fp16 / int8 can run as CTA pairs (M = 256 per MMA, each CTA holding half of B): opt-in
-    // with the environment variable DCNV2_PAIR=1. One CTA per tile is the default, measured
-    // faster on the 256-channel layers (the pair adds a cross-CTA hand-off to every K-block).
-    const char* pe = std::getenv("DCNV2_PAIR");
-    p.pair = (prec == PREC_F16 || prec == PREC_I8) && pe && pe[0] == '1' && pe[1] == 0;
+    // (override pair = 1). One CTA per tile is the default, measured faster on the
+    // 256-channel layers (the pair adds a cross-CTA hand-off to every K-block).
+    p.pair = (prec == PREC_F16 || prec == PREC_I8) && g_pair_override.load() == 1;
     p.a_stage_bytes = static_cast<uint32_t>(nA * kATileBytes);
     p.b_kb_bytes = size_t(nB) * p.nrows * kRowBytes;
     p.b_stage_bytes = static_cast<uint32_t>(p.b_kb_bytes / (p.pair ? 2 : 1));
@@ -338,12 +355,12 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
     }
   }
   // fp16 / int8 with at most 256 output channels take the kernel with the A operand in TMEM
-  // (environment DCNV2_KERNEL=smem keeps the shared-memory A kernel; DCNV2_KERNEL=ta also uses
-  // it for wider layers, one output-channel chunk of <= 256 per tile).
+  // (override "smem" keeps the shared-memory A kernel; "ta" also uses it for wider layers, one
+  // output-channel chunk of <= 256 per tile).
   if (p.fused && (prec == PREC_F16 || prec == PREC_I8)) {
-    const char* ke = std::getenv("DCNV2_KERNEL");
-    const bool force_smem = ke && std::strcmp(ke, "smem") == 0;
-    const bool force_ta = ke && std::strcmp(ke, "ta") == 0;
+    const int kov = g_kernel_override.load();
+    const bool force_smem = kov == KOV_SMEM;
+    const bool force_ta = kov == KOV_TA;
     if (!force_smem && (p.O <= 256 || force_ta)) {
       Plan t = p;
       plan_ta(&t);
@@ -377,10 +394,10 @@ bool set_smem_attr(F* kfn) {
                               static_cast<int>(kSmemLimit)) == cudaSuccess;
 }
 
-// Launch configuration of a grid of CTA pairs (clusters of 2 along x). The attribute lives in a
-// static array, so callers copy it before changing the configuration.
-cudaLaunchConfig_t pair_launch_config(int grid, size_t smem, cudaStream_t st) {
-  static cudaLaunchAttribute attr[1];
+// Launch configuration of a grid of CTA pairs (clusters of 2 along x). The cluster attribute is
+// written into the caller's `attr`, which must outlive the launch call.
+cudaLaunchConfig_t pair_launch_config(int grid, size_t smem, cudaStream_t st,
+                                      cudaLaunchAttribute (&attr)[1]) {
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
@@ -541,10 +558,9 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
       }
       if (p.pair) {
         const int nc = (p.num_tiles < di->sm_count / 2) ? p.num_tiles : di->sm_count / 2;
-        cudaLaunchConfig_t cfg = pair_launch_config(2 * nc, p.smem_bytes, st);
+        cudaLaunchAttribute at[1];
+        cudaLaunchConfig_t cfg = pair_launch_config(2 * nc, p.smem_bytes, st, at);
         cfg.blockDim = dim3(kTaThreads, 1, 1);
-        cudaLaunchAttribute at = cfg.attrs[0];
-        cfg.attrs = &at;
         e = cudaLaunchKernelEx(&cfg, kfn, a, tmap);
       } else {
         const int grid = p.num_tiles < di->sm_count ? p.num_tiles : di->sm_count;
@@ -564,9 +580,8 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
       int clusters = di->pair_clusters[PREC].load(std::memory_order_acquire);
       if (clusters <= 0) {
         // co-resident CTA pairs of this kernel (one CTA per SM); a persistent grid of that size
-        cudaLaunchConfig_t qc = pair_launch_config(1, p.smem_bytes, st);
-        cudaLaunchAttribute qa = qc.attrs[0];
-        qc.attrs = &qa;
+        cudaLaunchAttribute qa[1];
+        cudaLaunchConfig_t qc = pair_launch_config(1, p.smem_bytes, st, qa);
         if (cudaOccupancyMaxActiveClusters(&clusters, kfn, &qc) != cudaSuccess || clusters < 1) {
           cudaGetLastError();
           clusters = di->sm_count / 2;
@@ -574,9 +589,8 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
         di->pair_clusters[PREC].store(clusters, std::memory_order_release);
       }
       const int nc = p.num_tiles < clusters ? p.num_tiles : clusters;
-      cudaLaunchConfig_t cfg = pair_launch_config(2 * nc, p.smem_bytes, st);
-      cudaLaunchAttribute at = cfg.attrs[0];
-      cfg.attrs = &at;
+      cudaLaunchAttribute at[1];
+      cudaLaunchConfig_t cfg = pair_launch_config(2 * nc, p.smem_bytes, st, at);
       e = cudaLaunchKernelEx(&cfg, kfn, a, tmap);
       mk.mark(st);
       return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
@@ -854,6 +868,26 @@ dcnv2_status dcnv2_diag_timeout_selftest(uint32_t timeout_us, int32_t* device_co
   return v ? DCNV2_ERR_DEVICE_TIMEOUT : DCNV2_OK;
 }
 
+dcnv2_status dcnv2_diag_set_kernel_override(int32_t kernel, int32_t pair) {
+  if (kernel < KOV_AUTO || kernel > KOV_SMEM || pair < 0 || pair > 1)
+    return DCNV2_ERR_INVALID_ARG;
+  read_env_overrides();  // the environment is read first, so it never undoes this call
+  g_kernel_override.store(kernel);
+  g_pair_override.store(pair);
+  return DCNV2_OK;
+}
+
+dcnv2_status dcnv2_diag_binary_arch(int32_t* binary_version) {
+  if (!binary_version) return DCNV2_ERR_INVALID_ARG;
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, dcnv2_fused_ta_kernel<PREC_F16, false, 9, false>) != cudaSuccess) {
+    cudaGetLastError();
+    return DCNV2_ERR_NO_DEVICE;
+  }
+  *binary_version = fa.binaryVersion;
+  return DCNV2_OK;
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------------------------
@@ -1038,6 +1072,29 @@ static __device__ __align__(256) unsigned char dcnv2_static_scratch[DCNV2_STATIC
 namespace {
 std::mutex g_static_scratch_mu;
 void* g_static_scratch_addr[dcnv2::kMaxDevices] = {};
+
+// Device address of the static buffer on the current device, looked up once per device with that
+// device current (cudaGetSymbolAddress) and cached.
+dcnv2_status static_scratch_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return DCNV2_ERR_NO_DEVICE;
+  }
+  if (dev < 0 || dev >= dcnv2::kMaxDevices) return DCNV2_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (!g_static_scratch_addr[dev]) {
+    void* addr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&addr, dcnv2_static_scratch);
+    if (e != cudaSuccess || !addr) {
+      cudaGetLastError();
+      return DCNV2_ERR_CUDA;
+    }
+    g_static_scratch_addr[dev] = addr;
+  }
+  *out = g_static_scratch_addr[dev];
+  return DCNV2_OK;
+}
 }  // namespace
 
 extern "C" dcnv2_status dcnv2_forward_static_scratch(const dcnv2_desc* desc, const void* x,
@@ -1049,27 +1106,19 @@ extern "C" dcnv2_status dcnv2_forward_static_scratch(const dcnv2_desc* desc, con
   const dcnv2_status s = make_plan(desc, &p);
   if (s != DCNV2_OK) return s;
   if (p.ws_bytes > DCNV2_STATIC_SCRATCH_BYTES) return DCNV2_ERR_SCRATCH_LIMIT;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
-    cudaGetLastError();
-    return DCNV2_ERR_NO_DEVICE;
-  }
-  if (dev < 0 || dev >= dcnv2::kMaxDevices) return DCNV2_ERR_NO_DEVICE;
   void* scratch = nullptr;
-  {
-    // Once per device, with that device current: the device address of the static buffer.
-    std::lock_guard<std::mutex> lock(g_static_scratch_mu);
-    if (!g_static_scratch_addr[dev]) {
-      void* addr = nullptr;
-      const cudaError_t e = cudaGetSymbolAddress(&addr, dcnv2_static_scratch);
-      if (e != cudaSuccess || !addr) {
-        cudaGetLastError();
-        return DCNV2_ERR_CUDA;
-      }
-      g_static_scratch_addr[dev] = addr;
-    }
-    scratch = g_static_scratch_addr[dev];
-  }
+  const dcnv2_status a = static_scratch_address(&scratch);
+  if (a != DCNV2_OK) return a;
   return dcnv2_forward(desc, x, offset, mask, weight, bias, y, scratch,
                        DCNV2_STATIC_SCRATCH_BYTES, x_scale, w_scale, stream);
+}
+
+// The error word of the static buffer lies at its start (the buffer is 256-byte aligned, which is
+// where dcnv2_forward places the word of any workspace).
+extern "C" dcnv2_status dcnv2_read_static_scratch_error(dcnv2_stream_t stream, int32_t* code) {
+  if (!code) return DCNV2_ERR_INVALID_ARG;
+  void* scratch = nullptr;
+  const dcnv2_status a = static_scratch_address(&scratch);
+  if (a != DCNV2_OK) return a;
+  return dcnv2_read_device_error(scratch, stream, code);
 }

@@ -1,7 +1,8 @@
 """dcnv2_b200 — sm_100a DCNv2 forward behind the dcn::DCNv2 plugin interface.
 
-Importing this package loads libdcnv2.so (built by __graft_entry__.build()); the import fails
-if the library is missing, so no caller can silently run without the CUDA kernels.
+The first call into the library maps libdcnv2.so (built by __graft_entry__.build()); that call
+raises ImportError if the library is missing, so no caller can silently run without the CUDA
+kernels. Importing the package alone (e.g. for the seeded workload generators) maps nothing.
 """
 from .capi import DCNv2Error, DType, Math, Status, LIB_PATH  # noqa: F401
 from .plugin import (DCNv2Creator, DCNv2Plugin, FIELD_NAMES, PLUGIN_NAME,  # noqa: F401

@@ -2,8 +2,10 @@
 
 This is the Python-side FFI a caller of the reference would write around libdcnv2.so
 (python/02_build_and_validate.py:29 loads it with ctypes.CDLL). It adds nothing to the compute
-path: every forward goes through the C ABI into the sm_100a kernels. If the library is missing the
-import of this module fails loudly; there is no fallback.
+path: every forward goes through the C ABI into the sm_100a kernels. The library is mapped on the
+first call that needs it (so that importing the package's pure-Python parts, such as the
+workload generators, maps nothing); if it is missing that call raises ImportError. There is no
+fallback.
 """
 from __future__ import annotations
 
@@ -80,6 +82,9 @@ def _load() -> ctypes.CDLL:
         "dcnv2_forward_static_scratch": (ctypes.c_int, [Dp, P, P, P, P, P, P, ctypes.c_float,
                                                         ctypes.c_float, P]),
         "dcnv2_read_device_error": (ctypes.c_int, [P, P, ctypes.POINTER(ctypes.c_int32)]),
+        "dcnv2_read_static_scratch_error": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_int32)]),
+        "dcnv2_diag_set_kernel_override": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32]),
+        "dcnv2_diag_binary_arch": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32)]),
         "dcnv2_forward_host_workspace_size": (ctypes.c_size_t, [Dp, ctypes.c_int32]),
         "dcnv2_forward_host": (ctypes.c_int, [Dp, P, P, P, P, P, P, P, ctypes.c_size_t,
                                               ctypes.c_float, ctypes.c_float, ctypes.c_int32, P]),
@@ -121,12 +126,30 @@ def _load() -> ctypes.CDLL:
     return lib
 
 
-lib = _load()
+class _LazyLib:
+    """libdcnv2.so, mapped on first attribute access (ImportError if it is not built)."""
+
+    def __init__(self):
+        self._lib = None
+
+    def __getattr__(self, name):
+        if name.startswith("__"):
+            raise AttributeError(name)
+        if self._lib is None:
+            self._lib = _load()
+        return getattr(self._lib, name)
+
+    @property
+    def loaded(self) -> bool:
+        return self._lib is not None
+
+
+lib = _LazyLib()
 
 #: Every entry point include/dcnv2.h and include/dcnv2_diag.h declare.
 EXPORTED = (
     "dcnv2_output_shape", "dcnv2_workspace_size", "dcnv2_forward",
-    "dcnv2_forward_static_scratch", "dcnv2_read_device_error",
+    "dcnv2_forward_static_scratch", "dcnv2_read_static_scratch_error", "dcnv2_read_device_error",
     "dcnv2_forward_host_workspace_size", "dcnv2_forward_host",
     "dcnv2_uses_tensor_cores", "dcnv2_launch_count", "dcnv2_status_string", "dcnv2_plugin_name",
     "dcnv2_plugin_version", "dcnv2_plugin_namespace", "dcnv2_plugin_field_names",
@@ -134,7 +157,7 @@ EXPORTED = (
     "dcnv2_plugin_serialize", "dcnv2_plugin_nb_outputs", "dcnv2_plugin_output_dtype",
     "dcnv2_plugin_output_shape", "dcnv2_plugin_supports_format", "dcnv2_plugin_workspace_size",
     "dcnv2_plugin_enqueue", "dcnv2_diag_timeout_selftest", "dcnv2_diag_forward_events",
-    "dcnv2_diag_main_kernel",
+    "dcnv2_diag_main_kernel", "dcnv2_diag_set_kernel_override", "dcnv2_diag_binary_arch",
 )
 
 
@@ -226,3 +249,34 @@ def forward_static_scratch_raw(desc: Desc, x, offset, mask, weight, bias, y, x_s
     """Raw call of the allocation-free forward (scratch in the library's static buffer)."""
     return int(lib.dcnv2_forward_static_scratch(ctypes.byref(desc), x, offset, mask, weight, bias,
                                                 y, float(x_scale), float(w_scale), stream))
+
+
+def read_static_scratch_error(stream=0) -> int:
+    """Error word of the last dcnv2_forward_static_scratch call on the current device."""
+    code = ctypes.c_int32(0)
+    st = lib.dcnv2_read_static_scratch_error(stream, ctypes.byref(code))
+    if st not in (Status.OK, Status.ERR_DEVICE_TIMEOUT):
+        raise DCNv2Error(st, "dcnv2_read_static_scratch_error")
+    return int(code.value)
+
+
+class Kernel(enum.IntEnum):
+    """Kernel selection of dcnv2_diag_set_kernel_override."""
+    AUTO = 0
+    TA = 1     # A operand in tensor memory (dcnv2_fused_ta_kernel)
+    SMEM = 2   # A operand in shared memory (dcnv2_fused_kernel)
+
+
+def set_kernel_override(kernel: int = Kernel.AUTO, pair: bool = False) -> None:
+    st = lib.dcnv2_diag_set_kernel_override(int(kernel), 1 if pair else 0)
+    if st != Status.OK:
+        raise DCNv2Error(st, "dcnv2_diag_set_kernel_override")
+
+
+def binary_arch() -> int:
+    """cudaFuncAttributes::binaryVersion of the library's device code on the current device."""
+    v = ctypes.c_int32(0)
+    st = lib.dcnv2_diag_binary_arch(ctypes.byref(v))
+    if st != Status.OK:
+        raise DCNv2Error(st, "dcnv2_diag_binary_arch")
+    return int(v.value)

@@ -75,6 +75,16 @@ class Inputs:
     def tensors(self):
         return self.x, self.offset, self.mask, self.weight, self.bias
 
+    def images(self, start: int, stop: int) -> "Inputs":
+        """Images [start, stop) of the batch (x, offset, mask sliced; weight, bias shared)."""
+        L = self.layer
+        sub = Layer(stop - start, L.c, L.h, L.w, L.out_c, L.kernel, L.stride, L.padding,
+                    L.dilation, L.groups)
+        cut = lambda t: t[start:stop].contiguous()
+        return Inputs(sub, self.precision, cut(self.x), cut(self.offset), cut(self.mask),
+                      self.weight, self.bias, self.x_scale, self.w_scale,
+                      {k: (cut(v) if k == "x_f32" else v) for k, v in self.extra.items()})
+
     @property
     def input_bytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in self.tensors())

@@ -12,7 +12,7 @@ reference tree; the outputs are committed and the GPU tests only read them).
   npref_*.npz      the reference's own CPU forward (python/dcn_ort_op.py:68-92, imported from the
                    reference tree) on batch > 1 cases with deformable_groups = 1.
 
-Usage:  python tests/golden/gen_golden.py [--reference /root/reference]
+Usage:  python tests/golden/gen_golden.py --reference <reference project root>
 """
 import argparse
 import os
@@ -98,7 +98,8 @@ def npref_fixture(ref_python_dir, N, C, O, H, W, K, s, p, d, dg, ostd, outl, see
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="root of the reference project (holds python/dcn_ort_op.py)")
     args = ap.parse_args()
     kat = kat_fixture()
     print("kat y.sum =", float(kat["y"].sum()))

@@ -32,9 +32,30 @@ def test_library_exports_every_declared_symbol():
     assert names == set(capi.EXPORTED)
 
 
-def test_library_is_sm100a_only():
-    data = open(capi.LIB_PATH, "rb").read()
-    assert b"sm_100a" in data
+def test_library_build_targets_sm100a_only():
+    """The build recipe compiles every device object for sm_100a and nothing else (the device
+    code's architecture is checked at run time on the GPU: test_gpu_parity's
+    test_device_code_is_sm100)."""
+    mk = open(os.path.join(ROOT, "tensorrt-dcnv2-plugin_b200", "csrc", "Makefile")).read()
+    arch = re.findall(r"-gencode\s+arch=(\S+),code=(\S+)", mk)
+    assert arch == [("compute_100a", "sm_100a")]
+
+
+def test_package_import_maps_no_library():
+    """Importing the package (e.g. for the seeded workload generators) maps no libdcnv2.so; the
+    first library call does. The reference benchmark arm relies on this."""
+    import subprocess
+    import sys
+    code = ("import sys; sys.path.insert(0, %r)\n"
+            "import dcnv2_b200.workloads, dcnv2_b200\n"
+            "maps = open('/proc/self/maps').read()\n"
+            "assert 'libdcnv2.so' not in maps, 'mapped at import'\n"
+            "from dcnv2_b200 import capi\n"
+            "capi.lib.dcnv2_plugin_name()\n"
+            "assert 'libdcnv2.so' in open('/proc/self/maps').read()\n"
+            % os.path.join(ROOT, "tensorrt-dcnv2-plugin_b200"))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
 
 
 def test_plugin_identity_and_fields():

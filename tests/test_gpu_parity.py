@@ -281,6 +281,11 @@ def test_short_workspace_is_rejected_without_launch():
     assert bool((y == 7.0).all())  # nothing was launched
 
 
+def test_device_code_is_sm100():
+    """The runtime reports the library's device code as built for sm_100."""
+    assert capi.binary_arch() == 100
+
+
 def test_timeout_selftest_keeps_context_usable():
     st, code = capi.timeout_selftest(2000)  # a wait that nothing completes, 2 ms limit
     assert st == Status.ERR_DEVICE_TIMEOUT and code != 0
@@ -297,19 +302,27 @@ PAIR_SHAPES = {
 }
 
 
+@pytest.fixture
+def kernel_override():
+    """Sets the library's kernel selection for one test and restores automatic selection."""
+    yield capi.set_kernel_override
+    capi.set_kernel_override(capi.Kernel.AUTO, False)
+
+
 @pytest.mark.parametrize("shape", sorted(PAIR_SHAPES))
-def test_cta_pair_and_single_cta_paths_agree(shape, monkeypatch):
-    """fp16 / int8 run one CTA per 128-pixel tile by default; DCNV2_PAIR=1 selects CTA pairs
-    (cta_group::2, 256-pixel tiles). Both meet the stated bounds and agree with each other."""
+def test_cta_pair_and_single_cta_paths_agree(shape, kernel_override):
+    """fp16 / int8 run one CTA per 128-pixel tile by default; the pair override selects CTA
+    pairs (cta_group::2, 256-pixel tiles). Both meet the stated bounds and agree with each
+    other."""
     fx = random_case(**PAIR_SHAPES[shape])
     h = half_inputs(fx)
     ref16 = oracle.forward_ref(h["x"], h["offset"], h["mask"], h["weight"], h["bias"],
                                *oattrs(fx), precision="fp16")
     xq, xs, wq, ws = quantized(fx)
-    monkeypatch.setenv("DCNV2_PAIR", "1")
+    kernel_override(capi.Kernel.AUTO, True)
     y16_pair = run_fp16(fx)
     y8_pair = run_int8(fx, xq, xs, wq, ws)
-    monkeypatch.delenv("DCNV2_PAIR")
+    kernel_override(capi.Kernel.AUTO, False)
     y16_one = run_fp16(fx)
     y8_one = run_int8(fx, xq, xs, wq, ws)
     for y in (y16_pair, y16_one):
@@ -342,22 +355,20 @@ TA_SHAPES = {
 
 @pytest.mark.parametrize("pair", [False, True], ids=["cta", "pair"])
 @pytest.mark.parametrize("shape", sorted(TA_SHAPES))
-def test_tmem_a_kernel_matches_smem_a_kernel(shape, pair, monkeypatch):
-    """fp16 / int8 default to the kernel with the A operand in tensor memory
-    (DCNV2_KERNEL=ta also forces it for > 256 output channels); DCNV2_KERNEL=smem selects the
-    shared-memory A kernel. Both meet the stated bounds against the oracle and agree with each
-    other (same A values, same K order)."""
+def test_tmem_a_kernel_matches_smem_a_kernel(shape, pair, kernel_override):
+    """fp16 / int8 default to the kernel with the A operand in tensor memory (the "ta" override
+    also forces it for > 256 output channels); the "smem" override selects the shared-memory A
+    kernel. Both meet the stated bounds against the oracle and agree with each other (same A
+    values, same K order)."""
     fx = random_case(**TA_SHAPES[shape])
     h = half_inputs(fx)
     ref16 = oracle.forward_ref(h["x"], h["offset"], h["mask"], h["weight"], h["bias"],
                                *oattrs(fx), precision="fp16")
     xq, xs, wq, ws = quantized(fx)
-    if pair:
-        monkeypatch.setenv("DCNV2_PAIR", "1")
     out = {}
-    for kern in ("smem", "ta"):
-        monkeypatch.setenv("DCNV2_KERNEL", kern)
-        out[kern] = (run_fp16(fx), run_fp16(fx, Math.PRECISE), run_int8(fx, xq, xs, wq, ws))
+    for name, kern in (("smem", capi.Kernel.SMEM), ("ta", capi.Kernel.TA)):
+        kernel_override(kern, pair)
+        out[name] = (run_fp16(fx), run_fp16(fx, Math.PRECISE), run_int8(fx, xq, xs, wq, ws))
     for kern, (y16, y16p, y8) in out.items():
         assert mean_rel(y16, ref16) <= FP16_MEAN_REL, kern
         assert mean_rel(y16p, ref16) <= FP16_MEAN_REL, kern

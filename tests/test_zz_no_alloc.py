@@ -7,12 +7,15 @@ Two calls in a row go through the C ABI on one stream — a fp16 layer, then an 
 different shape that reuses the same buffer — and each output is checked against
 dcnv2_forward (own workspace) on the same inputs, with the tolerances of the parity tests
 (fp16: mean relative error <= 1e-3; int8: |dy| <= 1e-6 * (|acc*s| + |b|), here exact equality
-since the same kernels run). A problem larger than the buffer is refused before any launch.
-This file is named to be collected last and runs alone in a fresh process as well.
+since the same kernels run), and against the oracle with the same tolerances. The error word of
+the static buffer reads clear afterwards. A problem larger than the buffer is refused before any
+launch. This file is named to be collected last and runs alone in a fresh process as well.
 """
 import numpy as np
 import pytest
 import torch
+
+import oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -77,6 +80,19 @@ def test_static_scratch_matches_forward_on_two_calls_in_a_row():
     y8, r8 = outs[1].cpu().numpy().astype(np.float64), refs[1].cpu().numpy().astype(np.float64)
     bound = 1e-6 * (np.abs(r8) + 1.0)
     assert np.all(np.abs(y8 - r8) <= bound)
+    assert capi.read_static_scratch_error(stream) == 0
+    # the same outputs against the oracle
+    d16, t16 = cases[0][0], [v.float().cpu().numpy() for v in cases[0][1]]
+    ref16 = oracle.forward_ref(*t16, d16.stride, d16.padding, d16.dilation,
+                               d16.deformable_groups, precision="fp16")
+    assert float(np.abs(y16.cpu().numpy() - ref16).sum() / np.abs(ref16).sum()) <= 1e-3
+    d8, t8 = cases[1][0], [v.cpu().numpy() for v in cases[1][1]]
+    xs8, ws8 = cases[1][4], cases[1][5]
+    yx, acc = oracle.forward_i8_exact(t8[0], t8[1], t8[2], t8[3], t8[4], xs8, ws8, d8.stride,
+                                      d8.padding, d8.dilation, d8.deformable_groups)
+    s = float(np.float32(xs8) * np.float32(ws8))
+    denom = np.abs(acc.astype(np.float64) * s) + np.abs(t8[4]).reshape(1, -1, 1, 1)
+    assert np.all(np.abs(y8 - yx) <= 1e-6 * denom + 1e-30)
 
 
 def test_static_scratch_rejects_oversized_problem():
