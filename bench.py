@@ -67,6 +67,8 @@ def parse_args():
     ap.add_argument("--workload", default=HEADLINE, choices=list(wl.WORKLOADS))
     ap.add_argument("--global-batch", type=int, default=0,
                     help="split one batch of this many images over the ranks (strong scaling)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="images per rank instead of the workload's batch (small profiling cases)")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -533,12 +535,13 @@ def roofline_of(workload, inp, kname, per):
 
 # ---------------------------------------------------------------- one workload, measured
 def measure(workload, dist, device, stream, steps, warmup, e2e_steps, cpu_seconds, tv_seconds,
-            math=0, parts_cpu=None, with_clocks=False):
+            math=0, parts_cpu=None, with_clocks=False, n=None):
     """Times one workload on this rank's batch (all ranks take the same collective steps) and
-    returns its measurement dict; `parts_cpu` overrides the drawn inputs (the batch split)."""
+    returns its measurement dict; `parts_cpu` overrides the drawn inputs (the batch split), `n`
+    the workload's batch."""
     from dcnv2_b200 import capi
     if parts_cpu is None:
-        parts_cpu = wl.workload_parts(workload, seed=1000 * dist.rank)
+        parts_cpu = wl.workload_parts(workload, n=n, seed=1000 * dist.rank)
     parts = [p.to(device) for p in parts_cpu]
     bufs = [alloc_for(p, device, math) for p in parts]
     fns = [step_fn(p, ws, out, math) for p, (ws, out) in zip(parts, bufs)]
@@ -653,13 +656,15 @@ def run_ours(args, dist):
     if strong:
         parts_cpu, _ = split_inputs(args.workload, args.global_batch, dist)
     head = measure(args.workload, dist, device, stream, steps, warm, args.e2e_steps, cpu_s,
-                   min(cpu_s, 20.0), parts_cpu=parts_cpu, with_clocks=True)
-    batch_rank = (parts_cpu[0].layer.n if strong else parts_meta(args.workload)[0][0].n)
+                   min(cpu_s, 20.0), parts_cpu=parts_cpu, with_clocks=True,
+                   n=args.batch or None)
+    batch_rank = (parts_cpu[0].layer.n if strong
+                  else parts_meta(args.workload, args.batch or None)[0][0].n)
     global_batch = args.global_batch if strong else batch_rank * dist.world
 
     secondary = {}
     split = None
-    if not args.no_secondary and args.workload == HEADLINE and not strong:
+    if not args.no_secondary and args.workload == HEADLINE and not strong and not args.batch:
         sec_steps = max(20, steps // 20)
         sec_cpu = min(cpu_s, 4.0)
         # the headline layer with the fp32 sampler (one rounding per column value)

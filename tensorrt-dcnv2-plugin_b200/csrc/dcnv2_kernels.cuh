@@ -769,6 +769,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         item_from(t, dh, dw, m, wword, gpix);
       };
 
+      // No window (W too wide for one): for fp16 the cached item packs the corner's pixel index
+      // in the image (< 2^16) beside its weight instead of a window offset (block-uniform).
+      const bool gpacked = kPacked && !args.use_win && args.H * args.W <= 65536;
       for (int g = 0; g < args.dg && ok; ++g) {
         // items of every tap, computed once per (tile, group) for 3x3 kernels
         uint32_t cw[kCache];
@@ -794,6 +797,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             item_from(t, dh, dw, m, cw[t], cg[t]);
             // in the window: packed word's high half, else a negative (window) location
             inwin = inwin && (kPacked ? ((cw[t] >> 16) != kNoWin) : (cg[t] < 0));
+            if (gpacked) cw[t] = (cw[t] & 0xFFFFu) | (static_cast<uint32_t>(cg[t]) << 16);
           }
           // fp32 keeps the general path (two A tiles per K-block)
           fast_g = PREC != PREC_F32 && __all_sync(0xffffffffu, inwin);
@@ -889,13 +893,70 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (lane == 0) ptx::mbar_arrive(full_a + 8 * s);
               if (++s == S) { s = 0; ph ^= 1u; }
             }
+          } else if (KT > 0 && PREC != PREC_F32 && !args.use_win && (!kPacked || gpacked)) {
+            // No window (3x3): every corner is a 16-byte global load of the channels-last x.
+            // Straight-line per tap from the cached items (fp16: one shuffle of weight | pixel
+            // per corner; int8 / precise fp16: weight and pixel shuffled separately), 32-bit
+            // offsets inside the image, lanes past the group's channels predicated off (zeros).
+            const uint32_t row_bytes = static_cast<uint32_t>(args.C) * EB;
+#pragma unroll
+            for (int tt = 0; tt < kCache; ++tt) {
+              uint4 out[R];
+#pragma unroll
+              for (int r = 0; r < R; ++r) {
+                uint32_t wv[4];
+                uint4 xv[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  const int src = grp | (r * 4 + c);
+                  wv[c] = __shfl_sync(0xffffffffu, cw[tt], src);
+                  const uint32_t pix = kPacked ? (wv[c] >> 16)
+                                               : static_cast<uint32_t>(__shfl_sync(0xffffffffu, cg[tt], src));
+                  xv[c] = cvalid ? ptx::ld_nc_v4(gsrc + pix * row_bytes) : make_uint4(0, 0, 0, 0);
+                }
+                if (kPacked) {
+                  const __half2 w0 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[0])));
+                  const __half2 w1 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[1])));
+                  const __half2 w2 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[2])));
+                  const __half2 w3 = __half2half2(__ushort_as_half(static_cast<unsigned short>(wv[3])));
+                  out[r].x = f16_mix_h2(w0, w1, w2, w3, xv[0].x, xv[1].x, xv[2].x, xv[3].x);
+                  out[r].y = f16_mix_h2(w0, w1, w2, w3, xv[0].y, xv[1].y, xv[2].y, xv[3].y);
+                  out[r].z = f16_mix_h2(w0, w1, w2, w3, xv[0].z, xv[1].z, xv[2].z, xv[3].z);
+                  out[r].w = f16_mix_h2(w0, w1, w2, w3, xv[0].w, xv[1].w, xv[2].w, xv[3].w);
+                } else {
+                  const float wf4[4] = {__uint_as_float(wv[0]), __uint_as_float(wv[1]),
+                                        __uint_as_float(wv[2]), __uint_as_float(wv[3])};
+                  if (PREC == PREC_I8) {
+                    out[r].x = i8_mix_word(wf4, xv[0].x, xv[1].x, xv[2].x, xv[3].x);
+                    out[r].y = i8_mix_word(wf4, xv[0].y, xv[1].y, xv[2].y, xv[3].y);
+                    out[r].z = i8_mix_word(wf4, xv[0].z, xv[1].z, xv[2].z, xv[3].z);
+                    out[r].w = i8_mix_word(wf4, xv[0].w, xv[1].w, xv[2].w, xv[3].w);
+                  } else {
+                    out[r].x = f16_mix_precise(wf4, xv[0].x, xv[1].x, xv[2].x, xv[3].x);
+                    out[r].y = f16_mix_precise(wf4, xv[0].y, xv[1].y, xv[2].y, xv[3].y);
+                    out[r].z = f16_mix_precise(wf4, xv[0].z, xv[1].z, xv[2].z, xv[3].z);
+                    out[r].w = f16_mix_precise(wf4, xv[0].w, xv[1].w, xv[2].w, xv[3].w);
+                  }
+                  if (!cvalid) out[r] = make_uint4(0, 0, 0, 0);
+                }
+              }
+              const bool got =
+                  wait_bar<kSuspend>(empty + 8 * s, ph ^ 1, wc, DCNV2_DEVERR_TIMEOUT_SAMPLER);
+              if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+              const uint32_t a_s = a_base + s * args.a_stage_bytes;
+#pragma unroll
+              for (int r = 0; r < R; ++r) ptx::st_shared_v4(a_s + dst_off[r], out[r]);
+              ptx::fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) ptx::mbar_arrive(full_a + 8 * s);
+              if (++s == S) { s = 0; ph ^= 1u; }
+            }
           } else {
             // General path (any tap count, corners outside the window, partial chunks, int8,
-            // fp32 and precise fp16): items recomputed per K-block.
-            for (int t = 0; t < T && ok; ++t) {
-              uint32_t myw;
-              int myg;
-              item(g, t, myw, myg);
+            // fp32 and precise fp16). For 3x3 kernels the items come from the per-(tile, group)
+            // cache computed above (no geometry load in the K-block loop: a warp's K-block waits
+            // on one round trip, its corner loads); otherwise they are recomputed per K-block.
+            auto general_kblock = [&](uint32_t myw, int myg) -> bool {
               uint32_t wv[R][4];
               int loc[R][4];  // >= 0: window byte offset; < 0: global pixel -loc - 1
 #pragma unroll
@@ -907,7 +968,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const int gp = __shfl_sync(0xffffffffu, myg, src);
                   if (kPacked) {
                     wv[r][c] = v;
-                    loc[r][c] = (v >> 16) != kNoWin ? static_cast<int>(v >> 16) : -gp - 1;
+                    loc[r][c] = (KT > 0 && gpacked) ? -static_cast<int>(v >> 16) - 1
+                                : (v >> 16) != kNoWin ? static_cast<int>(v >> 16) : -gp - 1;
                   } else {
                     wv[r][c] = v;
                     loc[r][c] = gp < 0 ? (-gp - 1) * kRowBytes : -gp - 1;
@@ -967,7 +1029,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
               const bool got =
                   wait_bar<kSuspend>(empty + 8 * s, ph ^ 1, wc, DCNV2_DEVERR_TIMEOUT_SAMPLER);
-              if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+              if (!__all_sync(0xffffffffu, got)) return false;
               const uint32_t a_s = a_base + s * args.a_stage_bytes;
 #pragma unroll
               for (int r = 0; r < R; ++r) {
@@ -978,6 +1040,21 @@ __global__ void __launch_bounds__(kThreads, 1)
               __syncwarp();
               if (lane == 0) ptx::mbar_arrive(full_a + 8 * s);
               if (++s == S) { s = 0; ph ^= 1u; }
+              return true;
+            };
+            if constexpr (KT > 0) {
+#pragma unroll
+              for (int tt = 0; tt < kCache; ++tt) {
+                ok = general_kblock(cw[tt], cg[tt]);
+                if (!ok) break;
+              }
+            } else {
+              for (int t = 0; t < T && ok; ++t) {
+                uint32_t myw;
+                int myg;
+                item(g, t, myw, myg);
+                ok = general_kblock(myw, myg);
+              }
             }
           }
           if (!ok) break;
