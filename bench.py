@@ -67,6 +67,8 @@ def parse_args():
     ap.add_argument("--workload", default=HEADLINE, choices=list(wl.WORKLOADS))
     ap.add_argument("--global-batch", type=int, default=0,
                     help="split one batch of this many images over the ranks (strong scaling)")
+    ap.add_argument("--math", type=int, default=0,
+                    help="dcnv2_desc.math of the main workload (1 = DCNV2_MATH_PRECISE)")
     ap.add_argument("--batch", type=int, default=0,
                     help="images per rank instead of the workload's batch (small profiling cases)")
     ap.add_argument("--e2e-steps", type=int, default=20)
@@ -656,7 +658,7 @@ def run_ours(args, dist):
     if strong:
         parts_cpu, _ = split_inputs(args.workload, args.global_batch, dist)
     head = measure(args.workload, dist, device, stream, steps, warm, args.e2e_steps, cpu_s,
-                   min(cpu_s, 20.0), parts_cpu=parts_cpu, with_clocks=True,
+                   min(cpu_s, 20.0), math=args.math, parts_cpu=parts_cpu, with_clocks=True,
                    n=args.batch or None)
     batch_rank = (parts_cpu[0].layer.n if strong
                   else parts_meta(args.workload, args.batch or None)[0][0].n)
@@ -664,7 +666,8 @@ def run_ours(args, dist):
 
     secondary = {}
     split = None
-    if not args.no_secondary and args.workload == HEADLINE and not strong and not args.batch:
+    if (not args.no_secondary and args.workload == HEADLINE and not strong and not args.batch
+            and not args.math):
         sec_steps = max(20, steps // 20)
         sec_cpu = min(cpu_s, 4.0)
         # the headline layer with the fp32 sampler (one rounding per column value)

@@ -40,10 +40,12 @@ DCNV2_API const char* dcnv2_diag_main_kernel(const dcnv2_desc* desc);
 /* Kernel selection for measurements and tests, process-wide. kernel: 0 = automatic (A operand in
  * tensor memory for fp16 / int8 layers of at most 256 output channels, in shared memory above),
  * 1 = A in tensor memory for every fp16 / int8 layer (one output-channel chunk of at most 256 per
- * tile), 2 = A in shared memory always. pair: 1 = fp16 / int8 tiles run on CTA pairs
- * (tcgen05 cta_group::2), 0 = one CTA per tile (the default). The starting values come from the
- * environment, read once per process: DCNV2_KERNEL=ta|smem, DCNV2_PAIR=1. Change the selection
- * only between forwards: dcnv2_workspace_size and dcnv2_forward must see the same one. */
+ * tile), 2 = A in shared memory always. pair: 0 = automatic (CTA pairs, tcgen05 cta_group::2,
+ * for fp16 / int8 tiles of the A-in-shared-memory kernel with more than 256 output channels, one
+ * CTA per tile otherwise), 1 = CTA pairs for every fp16 / int8 tile, 2 = one CTA per tile always.
+ * The starting values come from the environment, read once per process: DCNV2_KERNEL=ta|smem,
+ * DCNV2_PAIR=1|0. Change the selection only between forwards: dcnv2_workspace_size and
+ * dcnv2_forward must see the same one. */
 DCNV2_API dcnv2_status dcnv2_diag_set_kernel_override(int32_t kernel, int32_t pair);
 
 /* Architecture of the device code this library runs on the current device, as the runtime

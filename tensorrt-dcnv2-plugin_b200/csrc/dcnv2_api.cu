@@ -60,11 +60,12 @@ DevInfo* device_info(int dev) {
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // Kernel-selection overrides for measurements and tests. They are read from the environment
-// once per process (DCNV2_KERNEL=ta|smem, DCNV2_PAIR=1) and can be changed afterwards only
+// once per process (DCNV2_KERNEL=ta|smem, DCNV2_PAIR=1|0) and can be changed afterwards only
 // through dcnv2_diag_set_kernel_override; the dispatch itself never calls getenv.
 enum { KOV_AUTO = 0, KOV_TA = 1, KOV_SMEM = 2 };
+enum { POV_AUTO = 0, POV_PAIRS = 1, POV_SINGLE = 2 };
 std::atomic<int> g_kernel_override{KOV_AUTO};
-std::atomic<int> g_pair_override{0};
+std::atomic<int> g_pair_override{POV_AUTO};
 std::once_flag g_env_once;
 void read_env_overrides() {
   std::call_once(g_env_once, []() {
@@ -72,7 +73,8 @@ void read_env_overrides() {
     if (ke && std::strcmp(ke, "smem") == 0) g_kernel_override.store(KOV_SMEM);
     else if (ke && std::strcmp(ke, "ta") == 0) g_kernel_override.store(KOV_TA);
     const char* pe = std::getenv("DCNV2_PAIR");
-    g_pair_override.store(pe && pe[0] == '1' && pe[1] == 0 ? 1 : 0);
+    if (pe && pe[0] == '1' && pe[1] == 0) g_pair_override.store(POV_PAIRS);
+    else if (pe && pe[0] == '0' && pe[1] == 0) g_pair_override.store(POV_SINGLE);
   });
 }
 
@@ -295,10 +297,14 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
     uint32_t cols = 32;
     while (cols < static_cast<uint32_t>(p.acc_bufs * p.nrows)) cols <<= 1;
     p.tmem_cols = cols;
-    // fp16 / int8 can run as CTA pairs (M = 256 per MMA, each CTA holding half of B): opt-in
-    // (override pair = 1). One CTA per tile is the default, measured faster on the
-    // 256-channel layers (the pair adds a cross-CTA hand-off to every K-block).
-    p.pair = (prec == PREC_F16 || prec == PREC_I8) && g_pair_override.load() == 1;
+    // fp16 / int8 run as CTA pairs (M = 256 per MMA, each CTA holding half of B) when a tile
+    // carries more than 256 output channels: each CTA then copies half of the 512-row weight
+    // tile per K-block, and four stages fit instead of two (512-channel dg8 layer: fp16
+    // 2.29 -> 2.20 ms, int8 2.31 -> 1.99 ms). Up to 256 channels one CTA per tile measured faster
+    // (the pair adds a cross-CTA hand-off to every K-block). The override forces either.
+    const int pov = g_pair_override.load();
+    p.pair = (prec == PREC_F16 || prec == PREC_I8) &&
+             (pov == POV_PAIRS || (pov == POV_AUTO && p.nsub >= 2));
     p.a_stage_bytes = static_cast<uint32_t>(nA * kATileBytes);
     p.b_kb_bytes = size_t(nB) * p.nrows * kRowBytes;
     p.b_stage_bytes = static_cast<uint32_t>(p.b_kb_bytes / (p.pair ? 2 : 1));
@@ -363,6 +369,7 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
     const bool force_ta = kov == KOV_TA;
     if (!force_smem && (p.O <= 256 || force_ta)) {
       Plan t = p;
+      t.pair = g_pair_override.load() == POV_PAIRS;  // the TMEM-A kernel pairs only when forced
       plan_ta(&t);
       if (t.ta) p = t;
     }
@@ -436,7 +443,9 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
            set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, false>) &&
            set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, true>) &&
            set_smem_attr(dcnv2_fused_ta_kernel<PREC, true, 0, false>) &&
-           set_smem_attr(dcnv2_fused_ta_kernel<PREC, true, 0, true>);
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, true, 0, true>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, true, 9, false>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, true, 9, true>);
     if constexpr (PREC == PREC_I8)
       ok = ok && set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, false>) &&
            set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, true>) &&
@@ -543,8 +552,10 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
     if (p.ta) {
       FusedFn kfn;
       if constexpr (PREC == PREC_F16) {
-        if (p.precise) kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, true, 0, true>
-                                    : dcnv2_fused_ta_kernel<PREC, true, 0, false>;
+        if (p.precise && k3) kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, true, 9, true>
+                                          : dcnv2_fused_ta_kernel<PREC, true, 9, false>;
+        else if (p.precise) kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, true, 0, true>
+                                         : dcnv2_fused_ta_kernel<PREC, true, 0, false>;
         else if (k3) kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, false, 9, true>
                                   : dcnv2_fused_ta_kernel<PREC, false, 9, false>;
         else kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, false, 0, true>
@@ -869,7 +880,7 @@ dcnv2_status dcnv2_diag_timeout_selftest(uint32_t timeout_us, int32_t* device_co
 }
 
 dcnv2_status dcnv2_diag_set_kernel_override(int32_t kernel, int32_t pair) {
-  if (kernel < KOV_AUTO || kernel > KOV_SMEM || pair < 0 || pair > 1)
+  if (kernel < KOV_AUTO || kernel > KOV_SMEM || pair < POV_AUTO || pair > POV_SINGLE)
     return DCNV2_ERR_INVALID_ARG;
   read_env_overrides();  // the environment is read first, so it never undoes this call
   g_kernel_override.store(kernel);

@@ -521,7 +521,9 @@ __global__ void __launch_bounds__(kTaThreads, 1)
     // chunk (32 x 16 bytes), mixes them and stores its row with one tcgen05.st; the store of a
     // K-block is published after the next K-block's loads and mix (one store in flight per warp).
     constexpr int EPC = TR::kChunkElems, KC = TR::kBlockElems, EB = TR::kElemBytes;
-    constexpr bool kFast = (!PRECISE && KT > 0);
+    // 3x3 fast path (cached tap geometry, rotated conflict-free corner loads): fp16 with
+    // packed-half mix or, PRECISE, with fp32 corner weights and the fp32 mix; int8.
+    constexpr bool kFast = KT > 0;
     constexpr int kMyTaps = kFast ? (KT + kTaTapGroups - 1) / kTaTapGroups : 1;
     constexpr uint32_t kNoWin = 0xFFFFu;
     const int sw = warp - kSampWarp0;
@@ -636,6 +638,7 @@ __global__ void __launch_bounds__(kTaThreads, 1)
         // fast path (3x3): the 4 corners of each of this warp's taps as
         // (16-bit weight | window byte offset of the corner pixel << 16)
         uint32_t cw[kMyTaps][4];
+        float cwf[PRECISE ? kMyTaps : 1][4];  // PRECISE: the fp32 corner weights
         bool fast_g = false;
         if (kFast) {
           float gv[3 * kMyTaps];
@@ -658,10 +661,13 @@ __global__ void __launch_bounds__(kTaThreads, 1)
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               inwin = inwin && (t >= T || loc[c] >= 0);
-              // fp16: the weight's fp16 bits; int8: its 16-bit fixed-point value
+              // fp16: the weight's fp16 bits; int8: its 16-bit fixed-point value; PRECISE: the
+              // fp32 weight is kept beside the word
               const uint32_t hb =
-                  PREC == PREC_F16 ? static_cast<uint32_t>(__half_as_ushort(__float2half_rn(wt[c])))
-                                   : i8_weight(wt[c]);
+                  PRECISE ? 0u
+                  : PREC == PREC_F16 ? static_cast<uint32_t>(__half_as_ushort(__float2half_rn(wt[c])))
+                                     : i8_weight(wt[c]);
+              if constexpr (PRECISE) cwf[u][c] = wt[c];
               cw[u][c] = hb | ((loc[c] >= 0 ? static_cast<uint32_t>(loc[c]) : kNoWin) << 16);
             }
           }
@@ -721,7 +727,12 @@ __global__ void __launch_bounds__(kTaThreads, 1)
                 // the previous K-block's TMEM store has had time to land: publish it now rather
                 // than after this whole K-block
                 if (h == 0) flush();
-                if (PREC == PREC_F16) {
+                if (PREC == PREC_F16 && PRECISE) {
+                  out[4 * h + 0] = f16_mix_precise(cwf[u], xv[0].x, xv[1].x, xv[2].x, xv[3].x);
+                  out[4 * h + 1] = f16_mix_precise(cwf[u], xv[0].y, xv[1].y, xv[2].y, xv[3].y);
+                  out[4 * h + 2] = f16_mix_precise(cwf[u], xv[0].z, xv[1].z, xv[2].z, xv[3].z);
+                  out[4 * h + 3] = f16_mix_precise(cwf[u], xv[0].w, xv[1].w, xv[2].w, xv[3].w);
+                } else if (PREC == PREC_F16) {
                   out[4 * h + 0] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].x, xv[1].x, xv[2].x, xv[3].x);
                   out[4 * h + 1] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].y, xv[1].y, xv[2].y, xv[3].y);
                   out[4 * h + 2] = f16_mix_h2(wh[0], wh[1], wh[2], wh[3], xv[0].z, xv[1].z, xv[2].z, xv[3].z);

@@ -267,8 +267,15 @@ class Kernel(enum.IntEnum):
     SMEM = 2   # A operand in shared memory (dcnv2_fused_kernel)
 
 
-def set_kernel_override(kernel: int = Kernel.AUTO, pair: bool = False) -> None:
-    st = lib.dcnv2_diag_set_kernel_override(int(kernel), 1 if pair else 0)
+class Pair(enum.IntEnum):
+    """CTA-pair selection of dcnv2_diag_set_kernel_override."""
+    AUTO = 0     # pairs for A-in-shared-memory tiles of more than 256 output channels
+    PAIRS = 1    # every fp16 / int8 tile on a CTA pair (tcgen05 cta_group::2)
+    SINGLE = 2   # one CTA per tile
+
+
+def set_kernel_override(kernel: int = Kernel.AUTO, pair: int = Pair.AUTO) -> None:
+    st = lib.dcnv2_diag_set_kernel_override(int(kernel), int(pair))
     if st != Status.OK:
         raise DCNv2Error(st, "dcnv2_diag_set_kernel_override")
 

@@ -306,23 +306,23 @@ PAIR_SHAPES = {
 def kernel_override():
     """Sets the library's kernel selection for one test and restores automatic selection."""
     yield capi.set_kernel_override
-    capi.set_kernel_override(capi.Kernel.AUTO, False)
+    capi.set_kernel_override(capi.Kernel.AUTO, capi.Pair.AUTO)
 
 
 @pytest.mark.parametrize("shape", sorted(PAIR_SHAPES))
 def test_cta_pair_and_single_cta_paths_agree(shape, kernel_override):
-    """fp16 / int8 run one CTA per 128-pixel tile by default; the pair override selects CTA
-    pairs (cta_group::2, 256-pixel tiles). Both meet the stated bounds and agree with each
-    other."""
+    """fp16 / int8 tiles run on one CTA (128 pixels) or on a CTA pair (cta_group::2, 256
+    pixels; automatic above 256 output channels in the shared-memory A kernel), forced here
+    both ways. Both meet the stated bounds and agree with each other."""
     fx = random_case(**PAIR_SHAPES[shape])
     h = half_inputs(fx)
     ref16 = oracle.forward_ref(h["x"], h["offset"], h["mask"], h["weight"], h["bias"],
                                *oattrs(fx), precision="fp16")
     xq, xs, wq, ws = quantized(fx)
-    kernel_override(capi.Kernel.AUTO, True)
+    kernel_override(capi.Kernel.AUTO, capi.Pair.PAIRS)
     y16_pair = run_fp16(fx)
     y8_pair = run_int8(fx, xq, xs, wq, ws)
-    kernel_override(capi.Kernel.AUTO, False)
+    kernel_override(capi.Kernel.AUTO, capi.Pair.SINGLE)
     y16_one = run_fp16(fx)
     y8_one = run_int8(fx, xq, xs, wq, ws)
     for y in (y16_pair, y16_one):
@@ -367,7 +367,7 @@ def test_tmem_a_kernel_matches_smem_a_kernel(shape, pair, kernel_override):
     xq, xs, wq, ws = quantized(fx)
     out = {}
     for name, kern in (("smem", capi.Kernel.SMEM), ("ta", capi.Kernel.TA)):
-        kernel_override(kern, pair)
+        kernel_override(kern, capi.Pair.PAIRS if pair else capi.Pair.SINGLE)
         out[name] = (run_fp16(fx), run_fp16(fx, Math.PRECISE), run_int8(fx, xq, xs, wq, ws))
     for kern, (y16, y16p, y8) in out.items():
         assert mean_rel(y16, ref16) <= FP16_MEAN_REL, kern
