@@ -638,6 +638,56 @@ def measure(workload, dist, device, stream, steps, warmup, e2e_steps, cpu_second
     return res
 
 
+def measure_head(dist, device, stream, steps, cpu_seconds):
+    """The headline layer with its offset / mask head (dcnv2_forward_with_head): one call per
+    step computes om = conv2d(x, Wh, bh) on tensor cores from the layer's channels-last x, splits
+    offset / sigmoid(mask) and runs the layer. Beside it: the layer alone on precomputed offsets
+    (dcnv2_forward) and the unfused head as a detector runs it without this fusion (torch
+    conv2d through cuDNN + slice + sigmoid, fp16), a library baseline."""
+    from dcnv2_b200 import capi
+    inp_cpu = wl.workload(HEADLINE, seed=1000 * dist.rank)
+    L = inp_cpu.layer
+    hw32, hb32 = wl.head_inputs(L, seed=1000 * dist.rank)
+    inp = inp_cpu.to(device)
+    hw, hb = hw32.half().to(device), hb32.half().to(device)
+    desc = desc_of(inp)
+    wsz = capi.forward_with_head_workspace_size(desc)
+    ws = torch.empty(wsz, dtype=torch.uint8, device=device)
+    y = torch.empty((L.n, L.out_c, L.ho, L.wo), dtype=torch.float16, device=device)
+    ptrs = [t.data_ptr() for t in (inp.x, hw, hb, inp.weight, inp.bias)]
+
+    def run(st):
+        rc = capi.forward_with_head_raw(desc, *ptrs, y.data_ptr(), None, None, ws.data_ptr(), wsz,
+                                        st)
+        if rc != 0:
+            raise RuntimeError(f"dcnv2_forward_with_head failed: {capi.status_string(rc)}")
+
+    ms = dist.max(time_steps(run, stream, steps, 5, dist))
+    ws2, out2 = alloc_for(inp, device)
+    _, _, run_plain = step_fn(inp, ws2, out2)
+    ms_plain = dist.max(time_steps(run_plain, stream, steps, 5, dist))
+    n_off = 2 * L.groups * L.kernel ** 2
+
+    def torch_head(_st):
+        with torch.cuda.stream(stream):
+            om = torch.nn.functional.conv2d(inp.x, hw, hb, padding=(L.kernel - 1) // 2)
+            om[:, :n_off].contiguous()
+            torch.sigmoid(om[:, n_off:])
+
+    ms_torch = dist.max(time_steps(torch_head, stream, steps, 5, dist))
+    head_flops = 2 * L.n * L.ho * L.wo * (3 * L.groups * L.kernel ** 2) * L.c * L.kernel ** 2
+    del ws, ws2, out2, y, inp
+    torch.cuda.empty_cache()
+    return {"value": round((L.flops + head_flops) * dist.world / (ms * 1e-3) / 1e12, 2),
+            "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+            "layer_alone_ms": round(ms_plain, 4), "head_ms": round(ms - ms_plain, 4),
+            "unfused_head_torch_cudnn_ms": round(ms_torch, 4),
+            "what": "om = conv2d(x, Wh[27,256,3,3], bh) + split + sigmoid fused in front of the "
+                    "256->256 64x64 N=64 fp16 layer (dcnv2_forward_with_head); head_ms = the "
+                    "call minus the layer alone; the unfused head through torch/cuDNN for "
+                    "comparison"}
+
+
 def split_inputs(workload, global_batch, dist):
     """This rank's slice of one seeded batch of `global_batch` images."""
     if global_batch < dist.world:
@@ -675,6 +725,8 @@ def run_ours(args, dist):
         r.pop("_clocks")
         r["math"] = "DCNV2_MATH_PRECISE (fp32 sampler arithmetic, the reference's rounding)"
         secondary[HEADLINE + "_precise"] = r
+        secondary[HEADLINE + "_with_head"] = measure_head(dist, device, stream, sec_steps,
+                                                          sec_cpu)
         for name in ("int8_n64_256c_64", "fp32_n1_256c_64", "fpn_fp16_b32", "big_512c_128_dg8",
                      "big_512c_128_dg8_int8"):
             big = name.startswith("big")

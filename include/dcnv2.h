@@ -104,6 +104,29 @@ DCNV2_API dcnv2_status dcnv2_forward(const dcnv2_desc* desc,
                            void* workspace, size_t workspace_bytes,
                            float x_scale, float w_scale, dcnv2_stream_t stream);
 
+/* ---- Layer with its offset / mask head ---- */
+
+/* Workspace bytes for dcnv2_forward_with_head (0 when the desc is not supported there). */
+DCNV2_API size_t dcnv2_forward_with_head_workspace_size(const dcnv2_desc* desc);
+
+/* The DCNv2 block as the reference's detector builds it (python/detector.py:44,50-52;
+ * python/01_oracle_and_export.py:42,46-48): om = Conv2d(C -> 3*dg*K*K, K x K, stride 1,
+ * padding (K-1)/2, with bias)(x), offset = om[:, :2*dg*K*K], mask = sigmoid(om[:, 2*dg*K*K:]),
+ * y = DCNv2(x, offset, mask, weight, bias). There the head is a separate convolution, slice and
+ * sigmoid in front of the plugin (the plugin's inputs 1 and 2, src/dcn_plugin.cpp:134); here it
+ * runs on tensor cores from the layer's own channels-last copy of x and writes offset and mask
+ * in the layout the layer then reads. Supported: fp16 (desc.dtype DCNV2_HALF, math DEFAULT or
+ * PRECISE), stride 1, dilation 1, padding (K-1)/2, C a multiple of 8, 3*dg*K*K <= 256;
+ * DCNV2_ERR_UNSUPPORTED otherwise. head_weight [3*dg*K*K][C][K][K] and head_bias [3*dg*K*K]
+ * (NULL = zeros) are fp16 device pointers. offset_out [N][2*dg*K*K][H][W] and mask_out
+ * [N][dg*K*K][H][W] (fp16, device) receive the head's outputs when not NULL; otherwise they stay
+ * in the workspace. Asynchronous on `stream`; never allocates or synchronises. */
+DCNV2_API dcnv2_status dcnv2_forward_with_head(const dcnv2_desc* desc, const void* x,
+                                               const void* head_weight, const void* head_bias,
+                                               const void* weight, const void* bias, void* y,
+                                               void* offset_out, void* mask_out, void* workspace,
+                                               size_t workspace_bytes, dcnv2_stream_t stream);
+
 /* ---- Host-buffer forward (copies overlapped with compute) ---- */
 
 /* Workspace bytes for dcnv2_forward_host with chunks of at most `images_per_chunk` images (0

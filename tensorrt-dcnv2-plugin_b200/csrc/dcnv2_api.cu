@@ -18,6 +18,7 @@
 #include "../../include/dcnv2.h"
 #include "../../include/dcnv2_diag.h"
 #include <cudaTypedefs.h>
+#include "dcnv2_head_kernel.cuh"
 #include "dcnv2_kernels.cuh"
 #include "dcnv2_ta_kernel.cuh"
 
@@ -419,10 +420,67 @@ cudaLaunchConfig_t pair_launch_config(int grid, size_t smem, cudaStream_t st,
   return cfg;
 }
 
+// The offset / mask head of dcnv2_forward_with_head: its packed weights, launch shape and
+// tensor map, launched by launch_fused between the layer's pre-passes and its main kernel.
+struct HeadLaunch {
+  HeadArgs a;
+  const void* weight = nullptr;  // [n_head][C][K][K] fp16
+  int cb = 0;                    // channel blocks of 64
+  size_t smem = 0;
+  int grid = 0;
+};
+
+dcnv2_status launch_head_pack(const HeadLaunch& h, DevInfo* di, cudaStream_t st, Marks& mk) {
+  const size_t total = size_t(h.a.numKB) * h.a.n_mma * 8;
+  int64_t blocks = cdiv(static_cast<int64_t>(total), 256);
+  const int64_t cap = int64_t(di->sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  mk.mark(st);
+  pack_weights_kernel<PREC_F16><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+      h.weight, const_cast<uint8_t*>(h.a.wpack), h.a.err, h.a.n_head, h.a.C, h.a.T, h.a.C, h.cb,
+      h.a.numKB, h.a.n_mma, 1, 0);
+  return cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
+}
+
+dcnv2_status launch_head(const HeadLaunch& h, DevInfo* di, const void* x_nhwc, cudaStream_t st,
+                         Marks& mk) {
+  constexpr uint32_t kHeadBit = 1u << 5;
+  if (!(di->attr_set.load(std::memory_order_acquire) & kHeadBit)) {
+    if (!set_smem_attr(dcnv2_offset_head_kernel)) {
+      cudaGetLastError();
+      return DCNV2_ERR_CUDA;
+    }
+    di->attr_set.fetch_or(kHeadBit, std::memory_order_acq_rel);
+  }
+  // channels-last x as bytes {C*2, W, H, N}; box = one 128-byte channel block of TR rows x TW
+  // columns, 128-byte swizzle (the MMA's A tile layout)
+  const HeadArgs& a = h.a;
+  const cuuint64_t dims[4] = {cuuint64_t(a.C) * 2, cuuint64_t(a.W), cuuint64_t(a.H),
+                              cuuint64_t(a.N)};
+  const cuuint64_t strides[3] = {cuuint64_t(a.C) * 2, cuuint64_t(a.W) * a.C * 2,
+                                 cuuint64_t(a.H) * a.W * a.C * 2};
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(kRowBytes), static_cast<cuuint32_t>(a.TW),
+                             static_cast<cuuint32_t>(a.TR), 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUtensorMap tmap;
+  std::memset(&tmap, 0, sizeof(tmap));
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode || encode(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(x_nhwc), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return DCNV2_ERR_CUDA;
+  mk.mark(st);
+  dcnv2_offset_head_kernel<<<h.grid, kHeadThreads, h.smem, st>>>(a, tmap);
+  return cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
+}
+
 template <int PREC>
 dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, const void* offset,
                           const void* mask, const void* weight, const void* bias, void* y,
-                          uint8_t* ws, float scale, cudaStream_t st, Marks& mk) {
+                          uint8_t* ws, float scale, cudaStream_t st, Marks& mk,
+                          const HeadLaunch* head = nullptr) {
   using TR = PrecTraits<PREC>;
   using XT = typename TR::X;
   constexpr bool kCanPair = PREC == PREC_F16 || PREC == PREC_I8;
@@ -497,6 +555,11 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
                                                     HW);
     }
   }
+  // 1b) the offset / mask head's weights (also clears the error word)
+  if (head) {
+    const dcnv2_status hs = launch_head_pack(*head, di, st, mk);
+    if (hs != DCNV2_OK) return hs;
+  }
   // 2) weights -> swizzled B tiles (also clears the error word)
   {
     const size_t total = size_t(p.cchunks) * p.numKB * p.nrows * 8;
@@ -508,6 +571,11 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
     pack_weights_kernel<PREC><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
         weight, wpack, err, p.O, p.C, p.T, p.Cg, p.CBg, p.numKB, p.nrows, p.cchunks,
         p.pair ? p.n_mma / 2 : 0);
+  }
+  // 2b) the offset / mask head from the channels-last x; the main kernel reads its outputs
+  if (head) {
+    const dcnv2_status hs = launch_head(*head, di, x_nhwc, st, mk);
+    if (hs != DCNV2_OK) return hs;
   }
   // 3) the fused implicit GEMM
   FusedArgs a;
@@ -809,6 +877,110 @@ dcnv2_status dcnv2_forward(const dcnv2_desc* desc, const void* x, const void* of
   Marks none;
   return forward_impl(desc, x, offset, mask, weight, bias, y, workspace, workspace_bytes, x_scale,
                       w_scale, stream, none);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Layer with its offset / mask head: om = Conv2d(C -> 3*dg*K*K, K, stride 1, padding (K-1)/2)(x)
+// on tensor cores from the layer's own channels-last copy of x, offset = om[:, :2*dg*K*K],
+// mask = sigmoid(om[:, 2*dg*K*K:]), then the deformable layer on them.
+namespace {
+
+struct HeadPlan {
+  Plan p;
+  HeadLaunch h;
+  size_t off_hw = 0, off_off = 0, off_msk = 0, total = 0;  // from the 256-aligned base
+};
+
+dcnv2_status make_head_plan(const dcnv2_desc* d, HeadPlan* hp) {
+  const dcnv2_status st = make_plan(d, &hp->p);
+  if (st != DCNV2_OK) return st;
+  const Plan& p = hp->p;
+  // fp16 layers on the tensor-core path; the head is a stride-1, dilation-1 "same" convolution,
+  // so the layer must have the same output size (stride 1, dilation 1, padding (K-1)/2)
+  if (p.prec != PREC_F16 || p.kind != KIND_TCGEN05) return DCNV2_ERR_UNSUPPORTED;
+  if (p.stride != 1 || p.dil != 1 || p.K % 2 == 0 || p.pad != (p.K - 1) / 2)
+    return DCNV2_ERR_UNSUPPORTED;
+  if (p.C % 8 != 0) return DCNV2_ERR_UNSUPPORTED;  // 16-byte rows of the channels-last copy
+  const int n_head = 3 * p.dg * p.T;
+  if (n_head > 256) return DCNV2_ERR_UNSUPPORTED;  // one MMA of N <= 256
+  HeadArgs& a = hp->h.a;
+  a = HeadArgs{};
+  a.N = p.N; a.C = p.C; a.H = p.H; a.W = p.W; a.K = p.K; a.pad = p.pad; a.T = p.T;
+  a.n_head = n_head;
+  a.n_off = 2 * p.dg * p.T;
+  a.n_mma = static_cast<int>(cdiv(n_head, 16) * 16);
+  hp->h.cb = static_cast<int>(cdiv(p.C, 64));
+  a.numKB = hp->h.cb * p.T;
+  int tw = 1;
+  while (tw < p.W && tw < kTileM) tw <<= 1;
+  a.TW = tw;
+  a.TR = kTileM / tw;
+  a.tiles_x = static_cast<int>(cdiv(p.W, a.TW));
+  a.tiles_y = static_cast<int>(cdiv(p.H, a.TR));
+  const int64_t tiles = int64_t(p.N) * a.tiles_x * a.tiles_y;
+  if (tiles >= (int64_t(1) << 31)) return DCNV2_ERR_INVALID_ARG;
+  a.num_tiles = static_cast<int>(tiles);
+  a.b_stage_bytes = static_cast<uint32_t>(a.n_mma) * kRowBytes;
+  uint32_t cols = 32;
+  while (cols < static_cast<uint32_t>(2 * a.n_mma)) cols <<= 1;
+  a.tmem_cols = cols;
+  const size_t fixed = 1024 + 256;  // alignment slack, barriers
+  int stages = static_cast<int>((kSmemLimit - fixed) / (kHeadABytes + a.b_stage_bytes));
+  a.stages = stages > kHeadMaxStages ? kHeadMaxStages : stages;
+  a.timeout_ns = kDefaultTimeoutNs;
+  hp->h.smem = fixed + size_t(a.stages) * (kHeadABytes + a.b_stage_bytes);
+  const size_t plane = size_t(p.H) * p.W;
+  size_t off = align_up(p.ws_bytes, 1024);
+  hp->off_hw = off;
+  off = align_up(off + size_t(a.numKB) * a.b_stage_bytes, 256);
+  hp->off_off = off;
+  off = align_up(off + size_t(p.N) * a.n_off * plane * 2, 256);
+  hp->off_msk = off;
+  off = align_up(off + size_t(p.N) * (n_head - a.n_off) * plane * 2, 256);
+  hp->total = off + 256;
+  return DCNV2_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t dcnv2_forward_with_head_workspace_size(const dcnv2_desc* desc) {
+  HeadPlan hp;
+  return make_head_plan(desc, &hp) == DCNV2_OK ? hp.total : 0;
+}
+
+dcnv2_status dcnv2_forward_with_head(const dcnv2_desc* desc, const void* x,
+                                     const void* head_weight, const void* head_bias,
+                                     const void* weight, const void* bias, void* y,
+                                     void* offset_out, void* mask_out, void* workspace,
+                                     size_t workspace_bytes, dcnv2_stream_t stream) {
+  HeadPlan hp;
+  const dcnv2_status s = make_head_plan(desc, &hp);
+  if (s != DCNV2_OK) return s;
+  if (!x || !head_weight || !weight || !y) return DCNV2_ERR_INVALID_ARG;
+  for (const void* ptr : {x, head_weight, head_bias, weight, bias, static_cast<const void*>(y),
+                          static_cast<const void*>(offset_out), static_cast<const void*>(mask_out)})
+    if (ptr && !aligned(ptr, 2)) return DCNV2_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < hp.total) return DCNV2_ERR_WORKSPACE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return DCNV2_ERR_NO_DEVICE; }
+  DevInfo* di = device_info(dev);
+  if (!di || !di->ok || di->major != 10) return DCNV2_ERR_NO_DEVICE;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(workspace), 256));
+  HeadArgs& a = hp.h.a;
+  a.wpack = ws + hp.off_hw;
+  a.bias = static_cast<const __half*>(head_bias);
+  a.offset = static_cast<__half*>(offset_out ? offset_out : ws + hp.off_off);
+  a.mask = static_cast<__half*>(mask_out ? mask_out : ws + hp.off_msk);
+  a.err = reinterpret_cast<int*>(ws);
+  hp.h.weight = head_weight;
+  hp.h.grid = a.num_tiles < di->sm_count ? a.num_tiles : di->sm_count;
+  Marks none;
+  return launch_fused<PREC_F16>(hp.p, di, dev, x, a.offset, a.mask, weight, bias, y, ws, 1.f,
+                                reinterpret_cast<cudaStream_t>(stream), none, &hp.h);
 }
 
 dcnv2_status dcnv2_diag_forward_events(const dcnv2_desc* desc, const void* x, const void* offset,

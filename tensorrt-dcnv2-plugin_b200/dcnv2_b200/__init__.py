@@ -7,8 +7,8 @@ kernels. Importing the package alone (e.g. for the seeded workload generators) m
 from .capi import DCNv2Error, DType, Math, Status, LIB_PATH  # noqa: F401
 from .plugin import (DCNv2Creator, DCNv2Plugin, FIELD_NAMES, PLUGIN_NAME,  # noqa: F401
                      PLUGIN_NAMESPACE, PLUGIN_VERSION, dcnv2_forward, dcnv2_forward_host,
-                     tensor_desc)
+                     dcnv2_forward_with_head, tensor_desc)
 
 __all__ = ["DCNv2Error", "DType", "Math", "Status", "DCNv2Creator", "DCNv2Plugin",
-           "dcnv2_forward", "dcnv2_forward_host", "tensor_desc", "PLUGIN_NAME", "PLUGIN_VERSION", "PLUGIN_NAMESPACE",
+           "dcnv2_forward", "dcnv2_forward_host", "dcnv2_forward_with_head", "tensor_desc", "PLUGIN_NAME", "PLUGIN_VERSION", "PLUGIN_NAMESPACE",
            "FIELD_NAMES", "LIB_PATH"]

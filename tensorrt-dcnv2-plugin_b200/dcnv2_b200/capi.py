@@ -85,6 +85,9 @@ def _load() -> ctypes.CDLL:
         "dcnv2_read_static_scratch_error": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_int32)]),
         "dcnv2_diag_set_kernel_override": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32]),
         "dcnv2_diag_binary_arch": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32)]),
+        "dcnv2_forward_with_head_workspace_size": (ctypes.c_size_t, [Dp]),
+        "dcnv2_forward_with_head": (ctypes.c_int, [Dp, P, P, P, P, P, P, P, P, P,
+                                                   ctypes.c_size_t, P]),
         "dcnv2_forward_host_workspace_size": (ctypes.c_size_t, [Dp, ctypes.c_int32]),
         "dcnv2_forward_host": (ctypes.c_int, [Dp, P, P, P, P, P, P, P, ctypes.c_size_t,
                                               ctypes.c_float, ctypes.c_float, ctypes.c_int32, P]),
@@ -150,6 +153,7 @@ lib = _LazyLib()
 EXPORTED = (
     "dcnv2_output_shape", "dcnv2_workspace_size", "dcnv2_forward",
     "dcnv2_forward_static_scratch", "dcnv2_read_static_scratch_error", "dcnv2_read_device_error",
+    "dcnv2_forward_with_head_workspace_size", "dcnv2_forward_with_head",
     "dcnv2_forward_host_workspace_size", "dcnv2_forward_host",
     "dcnv2_uses_tensor_cores", "dcnv2_launch_count", "dcnv2_status_string", "dcnv2_plugin_name",
     "dcnv2_plugin_version", "dcnv2_plugin_namespace", "dcnv2_plugin_field_names",
@@ -287,3 +291,15 @@ def binary_arch() -> int:
     if st != Status.OK:
         raise DCNv2Error(st, "dcnv2_diag_binary_arch")
     return int(v.value)
+
+
+def forward_with_head_workspace_size(desc: Desc) -> int:
+    return int(lib.dcnv2_forward_with_head_workspace_size(ctypes.byref(desc)))
+
+
+def forward_with_head_raw(desc: Desc, x, head_weight, head_bias, weight, bias, y, offset_out,
+                          mask_out, workspace, workspace_bytes, stream=0) -> int:
+    """Raw call of the layer with its offset / mask head; returns the dcnv2_status value."""
+    return int(lib.dcnv2_forward_with_head(ctypes.byref(desc), x, head_weight, head_bias, weight,
+                                           bias, y, offset_out, mask_out, workspace,
+                                           workspace_bytes, stream))

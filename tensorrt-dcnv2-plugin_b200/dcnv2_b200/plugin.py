@@ -248,3 +248,49 @@ def dcnv2_forward_host(x, offset, mask, weight, bias=None, stride: int = 1, padd
     if synchronize:
         torch.cuda.ExternalStream(stream, device=weight.device).synchronize()
     return out
+
+
+def dcnv2_forward_with_head(x, head_weight, head_bias, weight, bias=None, deformable_groups: int = 1,
+                            math: int = Math.DEFAULT, return_offsets: bool = False, out=None,
+                            workspace=None, stream=None):
+    """The DCNv2 block with its offset / mask head (python/detector.py:44,50-52 of the
+    reference): om = conv2d(x, head_weight, head_bias, padding=(K-1)//2), offset = om[:, :2*dg*K*K],
+    mask = sigmoid(om[:, 2*dg*K*K:]), y = DCNv2(x, offset, mask, weight, bias), all on the GPU
+    through dcnv2_forward_with_head (fp16, stride 1, dilation 1). Returns y, or
+    (y, offset, mask) with return_offsets."""
+    import torch
+    if x.dtype != torch.float16:
+        raise TypeError("dcnv2_forward_with_head runs fp16 layers")
+    N, C, H, W = (int(v) for v in x.shape)
+    O, K = int(weight.shape[0]), int(weight.shape[2])
+    desc = capi.make_desc(N, C, H, W, O, K, 1, (K - 1) // 2, 1, deformable_groups, DType.HALF,
+                          math)
+    tens = (x, head_weight, weight) + tuple(t for t in (head_bias, bias) if t is not None)
+    for t in tens:
+        if not t.is_cuda or not t.is_contiguous() or t.dtype != torch.float16:
+            raise ValueError("dcnv2_forward_with_head expects contiguous fp16 CUDA tensors")
+    ws_bytes = capi.forward_with_head_workspace_size(desc)
+    if ws_bytes == 0:
+        raise DCNv2Error(Status.ERR_UNSUPPORTED, "dcnv2_forward_with_head_workspace_size")
+    n, o, ho, wo = capi.output_shape(desc)
+    if out is None:
+        out = torch.empty((n, o, ho, wo), dtype=torch.float16, device=x.device)
+    T = K * K
+    off = msk = None
+    if return_offsets:
+        off = torch.empty((N, 2 * deformable_groups * T, H, W), dtype=torch.float16,
+                          device=x.device)
+        msk = torch.empty((N, deformable_groups * T, H, W), dtype=torch.float16, device=x.device)
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+    if stream is None:
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+    st = capi.forward_with_head_raw(
+        desc, x.data_ptr(), head_weight.data_ptr(),
+        head_bias.data_ptr() if head_bias is not None else None, weight.data_ptr(),
+        bias.data_ptr() if bias is not None else None, out.data_ptr(),
+        off.data_ptr() if off is not None else None, msk.data_ptr() if msk is not None else None,
+        workspace.data_ptr(), workspace.numel(), stream)
+    if st != Status.OK:
+        raise DCNv2Error(st, "dcnv2_forward_with_head")
+    return (out, off, msk) if return_offsets else out

@@ -181,3 +181,20 @@ def workload_parts(name: str, n: Optional[int] = None, seed: int = 0):
     if name == "fpn_fp16_b32":
         return [workload(name, n=n, level=s, seed=seed) for s in FPN_LEVELS]
     return [workload(name, n=n, seed=seed)]
+
+
+def head_inputs(layer: Layer, offset_std: float = 0.1, mask_logit: float = 3.0, seed: int = 0):
+    """Weights of an offset / mask head Conv2d(C -> 3*dg*K*K, K, padding (K-1)/2) for `layer`,
+    drawn so that on x ~ N(0, 1) the offsets come out ~N(0, offset_std^2) and the mask logits
+    ~N(mask_logit, offset_std^2) (the fp16 workload's identity-like distributions): weight
+    uniform with that standard deviation over the fan-in, bias 0 for the offsets and mask_logit
+    for the mask. Returned as fp32 CPU tensors ([3*dg*K*K, C, K, K], [3*dg*K*K])."""
+    g = torch.Generator().manual_seed(seed + 7919)
+    L = layer
+    n_head = 3 * L.groups * L.kernel ** 2
+    fan_in = L.c * L.kernel ** 2
+    bound = offset_std * math.sqrt(3.0 / fan_in)  # uniform(-b, b) has std b / sqrt(3)
+    w = (torch.rand((n_head, L.c, L.kernel, L.kernel), generator=g) * 2 - 1) * bound
+    b = torch.zeros(n_head)
+    b[2 * L.groups * L.kernel ** 2:] = mask_logit
+    return w, b

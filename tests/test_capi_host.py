@@ -202,3 +202,22 @@ def test_enqueue_rejects_mismatched_output_and_combination():
     mixed[1] = tensor_desc((1, 18, 8, 8), DType.FLOAT)
     assert p.enqueue(mixed, [tensor_desc((1, 8, 8, 8), H)], [256] * 5, [256], 256, 1 << 20) == \
         Status.ERR_UNSUPPORTED
+
+
+def test_forward_with_head_support_rules():
+    """The layer-with-head entry point takes fp16 "same" layers (stride 1, dilation 1, padding
+    (K-1)/2, C a multiple of 8, 3*dg*K*K <= 256) on the tensor-core path; its workspace holds the
+    layer's workspace plus the head's packed weights and its offset / mask outputs."""
+    ok = capi.make_desc(2, 64, 24, 24, 48, 3, 1, 1, 1, 1, DType.HALF)
+    need = capi.forward_with_head_workspace_size(ok)
+    assert need > capi.workspace_size(ok) + 2 * 27 * 24 * 24 * 2
+    for bad in (capi.make_desc(2, 64, 24, 24, 48, 3, 1, 1, 1, 1, DType.FLOAT),
+                capi.make_desc(2, 64, 24, 24, 48, 3, 1, 1, 1, 1, DType.INT8),
+                capi.make_desc(2, 64, 24, 24, 48, 3, 2, 1, 1, 1, DType.HALF),
+                capi.make_desc(2, 64, 24, 24, 48, 3, 1, 2, 2, 1, DType.HALF),
+                capi.make_desc(2, 60, 24, 24, 48, 3, 1, 1, 1, 1, DType.HALF),
+                capi.make_desc(2, 64, 24, 24, 48, 3, 1, 0, 1, 1, DType.HALF),
+                capi.make_desc(2, 640, 24, 24, 48, 3, 1, 1, 1, 10, DType.HALF)):
+        assert capi.forward_with_head_workspace_size(bad) == 0
+    assert capi.forward_with_head_workspace_size(
+        capi.make_desc(1, 256, 64, 64, 256, 3, 1, 1, 1, 8, DType.HALF)) > 0
