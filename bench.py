@@ -71,6 +71,9 @@ def parse_args():
                     help="dcnv2_desc.math of the main workload (1 = DCNV2_MATH_PRECISE)")
     ap.add_argument("--batch", type=int, default=0,
                     help="images per rank instead of the workload's batch (small profiling cases)")
+    ap.add_argument("--head", action="store_true",
+                    help="time only the headline layer with its offset / mask head "
+                         "(dcnv2_forward_with_head) and print that entry")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -638,14 +641,14 @@ def measure(workload, dist, device, stream, steps, warmup, e2e_steps, cpu_second
     return res
 
 
-def measure_head(dist, device, stream, steps, cpu_seconds):
+def measure_head(dist, device, stream, steps, cpu_seconds, n=None):
     """The headline layer with its offset / mask head (dcnv2_forward_with_head): one call per
     step computes om = conv2d(x, Wh, bh) on tensor cores from the layer's channels-last x, splits
     offset / sigmoid(mask) and runs the layer. Beside it: the layer alone on precomputed offsets
     (dcnv2_forward) and the unfused head as a detector runs it without this fusion (torch
     conv2d through cuDNN + slice + sigmoid, fp16), a library baseline."""
     from dcnv2_b200 import capi
-    inp_cpu = wl.workload(HEADLINE, seed=1000 * dist.rank)
+    inp_cpu = wl.workload(HEADLINE, n=n, seed=1000 * dist.rank)
     L = inp_cpu.layer
     hw32, hb32 = wl.head_inputs(L, seed=1000 * dist.rank)
     inp = inp_cpu.to(device)
@@ -682,10 +685,10 @@ def measure_head(dist, device, stream, steps, cpu_seconds):
             "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
             "layer_alone_ms": round(ms_plain, 4), "head_ms": round(ms - ms_plain, 4),
             "unfused_head_torch_cudnn_ms": round(ms_torch, 4),
-            "what": "om = conv2d(x, Wh[27,256,3,3], bh) + split + sigmoid fused in front of the "
-                    "256->256 64x64 N=64 fp16 layer (dcnv2_forward_with_head); head_ms = the "
-                    "call minus the layer alone; the unfused head through torch/cuDNN for "
-                    "comparison"}
+            "what": f"om = conv2d(x, Wh[27,256,3,3], bh) + split + sigmoid fused in front of "
+                    f"the 256->256 64x64 N={L.n} fp16 layer (dcnv2_forward_with_head); head_ms = "
+                    f"the call minus the layer alone; the unfused head through torch/cuDNN for "
+                    f"comparison"}
 
 
 def split_inputs(workload, global_batch, dist):
@@ -889,6 +892,15 @@ def main():
         return
     dist.init("nccl")
     try:
+        if args.head:
+            device = torch.device(f"cuda:{dist.local}")
+            torch.cuda.set_device(device)
+            r = measure_head(dist, device, torch.cuda.Stream(device), args.steps, 0.0,
+                             n=args.batch or None)
+            if dist.rank == 0:
+                print(json.dumps({"metric": "DCNv2 layer with offset/mask head, fp16",
+                                  "n_gpus": dist.world, "steps": args.steps, **r}), flush=True)
+            return
         run_ours(args, dist)
     finally:
         dist.close()
