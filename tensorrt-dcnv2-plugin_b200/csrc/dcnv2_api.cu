@@ -134,6 +134,8 @@ struct Plan {
   bool ta = false;
   int a_stages = 0, b_stages = 0;
   uint32_t win_stride = 0;
+  // int8 groups of 64 channels (half of a 128-byte K-block): two taps per K-block
+  bool tap_pairs = false;
 };
 
 int prec_of(int dtype) {
@@ -375,6 +377,14 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
       if (t.ta) p = t;
     }
   }
+  // int8 3x3 layers of the A-in-shared-memory kernel whose groups hold 64 channels (half of the
+  // 128-byte int8 K-block) and that run without a window: two taps per K-block (channels of tap
+  // 2i in bytes 0-63, of tap 2i+1 in bytes 64-127), 5 K-blocks per group instead of 9 half-empty
+  // ones.
+  if (p.fused && !p.ta && prec == PREC_I8 && !p.use_win && p.T == 9 && p.Cg == 64) {
+    p.tap_pairs = true;
+    p.numKB = p.dg * ((p.T + 1) / 2);
+  }
   // Workspace: [error word | x channels-last | packed weights]; +256 so that any base pointer
   // can be aligned up to 256 bytes.
   if (p.fused) p.kind = KIND_TCGEN05;
@@ -439,7 +449,7 @@ dcnv2_status launch_head_pack(const HeadLaunch& h, DevInfo* di, cudaStream_t st,
   mk.mark(st);
   pack_weights_kernel<PREC_F16><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
       h.weight, const_cast<uint8_t*>(h.a.wpack), h.a.err, h.a.n_head, h.a.C, h.a.T, h.a.C, h.cb,
-      h.a.numKB, h.a.n_mma, 1, 0);
+      h.a.numKB, h.a.n_mma, 1, 0, 0);
   return cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
 }
 
@@ -570,7 +580,7 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
     mk.mark(st);
     pack_weights_kernel<PREC><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
         weight, wpack, err, p.O, p.C, p.T, p.Cg, p.CBg, p.numKB, p.nrows, p.cchunks,
-        p.pair ? p.n_mma / 2 : 0);
+        p.pair ? p.n_mma / 2 : 0, p.tap_pairs ? 1 : 0);
   }
   // 2b) the offset / mask head from the channels-last x; the main kernel reads its outputs
   if (head) {
@@ -592,6 +602,7 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
   a.timeout_ns = kDefaultTimeoutNs;
   a.use_win = 0; a.win_rows = p.win_rows; a.win_top = p.win_top; a.win_bytes = p.win_bytes;
   a.win_stride = p.win_stride; a.a_stages = p.a_stages; a.b_stages = p.b_stages;
+  a.tap_pairs = p.tap_pairs ? 1 : 0;
   CUtensorMap tmap;
   std::memset(&tmap, 0, sizeof(tmap));
   if (p.use_win) {

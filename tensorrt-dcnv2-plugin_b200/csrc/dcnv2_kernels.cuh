@@ -92,6 +92,7 @@ struct FusedArgs {
   uint32_t win_bytes;      // win_rows * W * 128
   uint32_t win_stride;     // distance of the two window buffers (win_bytes rounded up to 1 KB)
   int a_stages, b_stages;  // A operand in TMEM: A ring (TMEM) and B ring (shared memory) depths
+  int tap_pairs;           // int8, 64-channel groups: K-block = taps (2i, 2i+1) x 64 channels
   int precise;             // fp16: fp32 sampler arithmetic
   int tf32_single;         // fp32: hi*hi only (plain TF32)
   unsigned long long timeout_ns;
@@ -893,6 +894,50 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (lane == 0) ptx::mbar_arrive(full_a + 8 * s);
               if (++s == S) { s = 0; ph ^= 1u; }
             }
+          } else if (KT > 0 && PREC == PREC_I8 && args.tap_pairs) {
+            // int8 with 64-channel groups, no window: K-block i holds taps 2i (chunks 0-3) and
+            // 2i+1 (chunks 4-7, zero past the last tap), so every lane loads and the group takes
+            // 5 K-blocks instead of 9 half-empty ones. Lane j takes the items of its own tap.
+            const uint32_t row_bytes = static_cast<uint32_t>(args.C) * EB;
+            const bool hi = j >= 4;
+            const uint8_t* psrc = ximg + static_cast<size_t>(gbase + (j & 3) * EPC) * EB;
+#pragma unroll
+            for (int pp = 0; pp < (kCache + 1) / 2; ++pp) {
+              const int t0 = 2 * pp, t1 = 2 * pp + 1 < kCache ? 2 * pp + 1 : 2 * pp;
+              const bool lane_valid = !(hi && 2 * pp + 1 >= kCache);
+              uint4 out[R];
+#pragma unroll
+              for (int r = 0; r < R; ++r) {
+                float wf4[4];
+                uint4 xv[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  const int src = grp | (r * 4 + c);
+                  const uint32_t w0 = __shfl_sync(0xffffffffu, cw[t0], src);
+                  const uint32_t w1 = __shfl_sync(0xffffffffu, cw[t1], src);
+                  const int g0 = __shfl_sync(0xffffffffu, cg[t0], src);
+                  const int g1 = __shfl_sync(0xffffffffu, cg[t1], src);
+                  wf4[c] = __uint_as_float(hi ? w1 : w0);
+                  const uint32_t pix = static_cast<uint32_t>(hi ? g1 : g0);
+                  xv[c] = lane_valid ? ptx::ld_nc_v4(psrc + pix * row_bytes) : make_uint4(0, 0, 0, 0);
+                }
+                out[r].x = i8_mix_word(wf4, xv[0].x, xv[1].x, xv[2].x, xv[3].x);
+                out[r].y = i8_mix_word(wf4, xv[0].y, xv[1].y, xv[2].y, xv[3].y);
+                out[r].z = i8_mix_word(wf4, xv[0].z, xv[1].z, xv[2].z, xv[3].z);
+                out[r].w = i8_mix_word(wf4, xv[0].w, xv[1].w, xv[2].w, xv[3].w);
+                if (!lane_valid) out[r] = make_uint4(0, 0, 0, 0);
+              }
+              const bool got =
+                  wait_bar<kSuspend>(empty + 8 * s, ph ^ 1, wc, DCNV2_DEVERR_TIMEOUT_SAMPLER);
+              if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+              const uint32_t a_s = a_base + s * args.a_stage_bytes;
+#pragma unroll
+              for (int r = 0; r < R; ++r) ptx::st_shared_v4(a_s + dst_off[r], out[r]);
+              ptx::fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) ptx::mbar_arrive(full_a + 8 * s);
+              if (++s == S) { s = 0; ph ^= 1u; }
+            }
           } else if (KT > 0 && PREC != PREC_F32 && !args.use_win && (!kPacked || gpacked)) {
             // No window (3x3): every corner is a 16-byte global load of the channels-last x.
             // Straight-line per tap from the cached items (fp16: one shuffle of weight | pixel
@@ -1243,7 +1288,8 @@ __global__ void __launch_bounds__(256) pack_weights_kernel(const void* __restric
                                                            uint8_t* __restrict__ wpack,
                                                            int* err, int O, int C, int T,
                                                            int Cg, int CBg, int numKB,
-                                                           int nrows, int cchunks, int half_mma) {
+                                                           int nrows, int cchunks, int half_mma,
+                                                           int tap_pairs) {
   using TR = PrecTraits<PREC>;
   constexpr int EPC = TR::kChunkElems, KC = TR::kBlockElems;
   if (blockIdx.x == 0 && threadIdx.x == 0) *err = 0;
@@ -1255,9 +1301,12 @@ __global__ void __launch_bounds__(256) pack_weights_kernel(const void* __restric
     const size_t blk = (idx >> 3) / nrows;  // cc * numKB + kb
     const int kb = static_cast<int>(blk % numKB);
     const int cc = static_cast<int>(blk / numKB);
-    const int t = kb % T;
-    const int cbg = (kb / T) % CBg;
-    const int g = kb / (CBg * T);
+    // K order (group, channel block, tap); with tap_pairs (int8, 64-channel groups, CBg = 1)
+    // K-block (group, i) holds tap 2i in chunks 0-3 and tap 2i+1 in chunks 4-7
+    const int npairs = (T + 1) / 2;
+    const int t = tap_pairs ? 2 * (kb % npairs) + (jc >> 2) : kb % T;
+    const int cbg = tap_pairs ? 0 : (kb / T) % CBg;
+    const int g = tap_pairs ? kb / npairs : kb / (CBg * T);
     const int o = cc * nrows + row;
     const size_t tile_base = blk * TR::kNumBTiles * nrows * kRowBytes;
     // CTA pair (half_mma = n_mma / 2 > 0): rows [sub*n_mma + rk*half_mma, +half_mma) go to CTA
@@ -1275,8 +1324,8 @@ __global__ void __launch_bounds__(256) pack_weights_kernel(const void* __restric
     uint8_t* lb = reinterpret_cast<uint8_t*>(&lo);
 #pragma unroll
     for (int e = 0; e < EPC; ++e) {
-      const int cig = cbg * KC + jc * EPC + e;
-      if (o < O && cig < Cg) {
+      const int cig = tap_pairs ? (jc & 3) * EPC + e : cbg * KC + jc * EPC + e;
+      if (o < O && cig < Cg && t < T) {
         const size_t src = (static_cast<size_t>(o) * C + g * Cg + cig) * T + t;
         if (PREC == PREC_F16) {
           reinterpret_cast<__half*>(hb)[e] = reinterpret_cast<const __half*>(w)[src];

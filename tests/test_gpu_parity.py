@@ -350,6 +350,9 @@ TA_SHAPES = {
     "c32_o24_s2": dict(n=3, c=32, o=24, h=33, w=29, s=2),
     # W > 256: no x window, every corner from global memory
     "c16_o32_w300": dict(n=1, c=16, o=32, h=5, w=300),
+    # no window, int8 groups of 64 channels: the shared-memory A kernel packs two taps per
+    # K-block (the TMEM-A kernel does not); both give the same integers
+    "c128_o48_dg2_w300": dict(n=2, c=128, o=48, h=5, w=300, dg=2, ostd=1.5),
 }
 
 
