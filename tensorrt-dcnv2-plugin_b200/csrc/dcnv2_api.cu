@@ -527,60 +527,44 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
   XT* x_nhwc = reinterpret_cast<XT*>(ws + p.off_x);
   uint8_t* wpack = ws + p.off_w;
 
-  // 1) x: NCHW -> NHWC
+  // 1) one launch: x NCHW -> channels-last (tiled kernels where the channel and pixel counts
+  // allow, the generic tile otherwise) and the weights -> swizzled B tiles (also clears the
+  // error word)
   {
-    constexpr int TILE = 32 * (4 / sizeof(XT));
     const int HW = p.H * p.W;
-    dim3 grid(static_cast<unsigned>(cdiv(HW, TILE)), static_cast<unsigned>(cdiv(p.C, TILE)),
-              static_cast<unsigned>(p.N));
-    const bool i8_tiles = sizeof(XT) == 1 && p.C % 128 == 0 && HW % 128 == 0 &&
-                          (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
-                          (reinterpret_cast<uintptr_t>(x_nhwc) & 15u) == 0;
-    const bool f16_tiles = sizeof(XT) == 2 && p.C % 64 == 0 && HW % 128 == 0 &&
-                           (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+    const bool aligned16 = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
                            (reinterpret_cast<uintptr_t>(x_nhwc) & 15u) == 0;
-    if (f16_tiles && grid.z <= 65535u) {
-      mk.mark(st);
-      nchw_to_nhwc_f16_kernel<<<dim3(static_cast<unsigned>(HW / 128), static_cast<unsigned>(p.C / 64),
-                                     static_cast<unsigned>(p.N)), 256, 0, st>>>(
-          reinterpret_cast<const __half*>(x), reinterpret_cast<__half*>(x_nhwc), p.C, HW);
-    } else if (i8_tiles && grid.z <= 65535u) {
-      mk.mark(st);
-      nchw_to_nhwc_i8_kernel<<<dim3(static_cast<unsigned>(HW / 128), static_cast<unsigned>(p.C / 128),
-                                    static_cast<unsigned>(p.N)), 256, 0, st>>>(
-          reinterpret_cast<const int8_t*>(x), reinterpret_cast<int8_t*>(x_nhwc), p.C, HW);
-    } else if (grid.z > 65535u) {
-      // Split large batches into launches of at most 65535 images.
-      for (int n0 = 0; n0 < p.N; n0 += 65535) {
-        const int nb = p.N - n0 < 65535 ? p.N - n0 : 65535;
-        dim3 g2(grid.x, grid.y, static_cast<unsigned>(nb));
-        mk.mark(st);
-        nchw_to_nhwc_kernel<XT><<<g2, 256, 0, st>>>(
-            reinterpret_cast<const XT*>(x) + size_t(n0) * p.C * HW,
-            x_nhwc + size_t(n0) * p.C * HW, p.C, HW);
-      }
+    const bool tiled = aligned16 && HW % 128 == 0 &&
+                       ((PREC == PREC_F16 && p.C % 64 == 0) || (PREC == PREC_I8 && p.C % 128 == 0));
+    PrepassArgs pa;
+    pa.x = x; pa.xt = x_nhwc; pa.C = p.C; pa.HW = HW; pa.tiled = tiled ? 1 : 0;
+    if (tiled) {
+      pa.tiles_x = HW / 128;
+      pa.tiles_y = p.C / (PREC == PREC_F16 ? 64 : 128);
     } else {
-      mk.mark(st);
-      nchw_to_nhwc_kernel<XT><<<grid, 256, 0, st>>>(reinterpret_cast<const XT*>(x), x_nhwc, p.C,
-                                                    HW);
+      constexpr int TILE = 8 * (16 / static_cast<int>(sizeof(XT)));
+      pa.tiles_x = static_cast<int>(cdiv(HW, TILE));
+      pa.tiles_y = static_cast<int>(cdiv(p.C, TILE));
     }
+    const int64_t tr_blocks = int64_t(pa.tiles_x) * pa.tiles_y * p.N;
+    const size_t total = size_t(p.cchunks) * p.numKB * p.nrows * 8;
+    int64_t pk_blocks = cdiv(static_cast<int64_t>(total), 256);
+    const int64_t cap = int64_t(di->sm_count) * 8;
+    if (pk_blocks > cap) pk_blocks = cap;
+    if (pk_blocks < 1) pk_blocks = 1;
+    if (tr_blocks + pk_blocks >= (int64_t(1) << 31)) return DCNV2_ERR_INVALID_ARG;
+    pa.tr_blocks = static_cast<int>(tr_blocks);
+    pa.w = weight; pa.wpack = wpack; pa.err = err;
+    pa.O = p.O; pa.T = p.T; pa.Cg = p.Cg; pa.CBg = p.CBg; pa.numKB = p.numKB;
+    pa.nrows = p.nrows; pa.cchunks = p.cchunks; pa.half_mma = p.pair ? p.n_mma / 2 : 0;
+    pa.tap_pairs = p.tap_pairs ? 1 : 0;
+    mk.mark(st);
+    prepass_kernel<PREC><<<static_cast<unsigned>(tr_blocks + pk_blocks), 256, 0, st>>>(pa);
   }
   // 1b) the offset / mask head's weights (also clears the error word)
   if (head) {
     const dcnv2_status hs = launch_head_pack(*head, di, st, mk);
     if (hs != DCNV2_OK) return hs;
-  }
-  // 2) weights -> swizzled B tiles (also clears the error word)
-  {
-    const size_t total = size_t(p.cchunks) * p.numKB * p.nrows * 8;
-    int64_t blocks = cdiv(static_cast<int64_t>(total), 256);
-    const int64_t cap = int64_t(di->sm_count) * 8;
-    if (blocks > cap) blocks = cap;
-    if (blocks < 1) blocks = 1;
-    mk.mark(st);
-    pack_weights_kernel<PREC><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
-        weight, wpack, err, p.O, p.C, p.T, p.Cg, p.CBg, p.numKB, p.nrows, p.cchunks,
-        p.pair ? p.n_mma / 2 : 0, p.tap_pairs ? 1 : 0);
   }
   // 2b) the offset / mask head from the channels-last x; the main kernel reads its outputs
   if (head) {
@@ -834,6 +818,7 @@ int32_t dcnv2_launch_count(const dcnv2_desc* desc) {
   Plan p;
   if (make_plan(desc, &p) != DCNV2_OK) return 0;
   if (p.kind == KIND_SIMT) return 1;
+  if (p.kind == KIND_TCGEN05) return 2;  // pre-pass (transpose + weight packing), main kernel
   const int64_t zsplits = (p.N + 65534) / 65535;
   return static_cast<int32_t>(zsplits + 2);
 }

@@ -1140,14 +1140,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 // pixels (128-byte rows both ways: 64x64 fp16, 128x128 int8, 32x32 fp32). Rows of the shared
 // tile are padded by 4 bytes so that the column reads of the store phase spread over banks.
 template <typename T>
-__global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const T* __restrict__ x,
-                                                           T* __restrict__ xt, int C, int HW) {
+__device__ __forceinline__ void transpose_tile(const T* __restrict__ x, T* __restrict__ xt, int C,
+                                               int HW, int bx, int by, int n) {
   constexpr int V = 16 / sizeof(T);
   constexpr int TILE = 8 * V;
   constexpr int PAD = 4 / sizeof(T);
   __shared__ T tile[TILE][TILE + PAD];
-  const int n = blockIdx.z;
-  const int c0 = blockIdx.y * TILE, p0 = blockIdx.x * TILE;
+  const int c0 = by * TILE, p0 = bx * TILE;
   const T* xs = x + static_cast<size_t>(n) * C * HW;
   T* xd = xt + static_cast<size_t>(n) * C * HW;
   const bool vec_in = (HW % V) == 0 && (p0 + TILE) <= HW &&
@@ -1190,6 +1189,11 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const T* __restrict__
     }
   }
 }
+template <typename T>
+__global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const T* __restrict__ x,
+                                                           T* __restrict__ xt, int C, int HW) {
+  transpose_tile<T>(x, xt, C, HW, blockIdx.x, blockIdx.y, blockIdx.z);
+}
 
 // int8 NCHW -> NHWC for C % 128 == 0 and H*W % 128 == 0 (16-byte aligned pointers): a tile of 128
 // channels x 128 pixels. Channel c of the tile sits in shared row (c % 16) * 8 + c / 16 (rows of
@@ -1197,13 +1201,12 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const T* __restrict__
 // Each thread turns 16 words (16 channels x 4 pixels) into 4 pixels x 16 channels with byte
 // permutes (4x4 byte transposes) and writes four 16-byte vectors; the 8 threads of one pixel
 // write its 128 channels contiguously.
-__global__ void __launch_bounds__(256) nchw_to_nhwc_i8_kernel(const int8_t* __restrict__ x,
-                                                              int8_t* __restrict__ xt, int C,
-                                                              int HW) {
+__device__ __forceinline__ void transpose_i8_tile(const int8_t* __restrict__ x,
+                                                  int8_t* __restrict__ xt, int C, int HW, int bx,
+                                                  int by, int n) {
   constexpr int kRowWords = 36;
   __shared__ __align__(16) uint32_t tile[128 * kRowWords];
-  const int n = blockIdx.z;
-  const int c0 = blockIdx.y * 128, p0 = blockIdx.x * 128;
+  const int c0 = by * 128, p0 = bx * 128;
   const int8_t* xs = x + static_cast<size_t>(n) * C * HW;
   int8_t* xd = xt + static_cast<size_t>(n) * C * HW;
   const int t = threadIdx.x;
@@ -1241,13 +1244,12 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_i8_kernel(const int8_t* __re
 // once fall in different bank groups. Each thread turns 8 words (8 channels x 2 pixels) into
 // 2 pixels x 8 channels with byte permutes and writes two 16-byte vectors; the 8 threads of one
 // pixel write its 64 channels contiguously.
-__global__ void __launch_bounds__(256) nchw_to_nhwc_f16_kernel(const __half* __restrict__ x,
-                                                               __half* __restrict__ xt, int C,
-                                                               int HW) {
+__device__ __forceinline__ void transpose_f16_tile(const __half* __restrict__ x,
+                                                   __half* __restrict__ xt, int C, int HW, int bx,
+                                                   int by, int n) {
   constexpr int kRowWords = 68;
   __shared__ __align__(16) uint32_t tile[64 * kRowWords];
-  const int n = blockIdx.z;
-  const int c0 = blockIdx.y * 64, p0 = blockIdx.x * 128;
+  const int c0 = by * 64, p0 = bx * 128;
   const __half* xs = x + static_cast<size_t>(n) * C * HW;
   __half* xd = xt + static_cast<size_t>(n) * C * HW;
   const int t = threadIdx.x;
@@ -1284,18 +1286,17 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_f16_kernel(const __half* __r
 // K-block kb = (g*CBg + cbg)*T + t holds channels g*Cg + cbg*KC + [0, KC) of tap t.
 // Also clears the device error word for the fused kernel that follows.
 template <int PREC>
-__global__ void __launch_bounds__(256) pack_weights_kernel(const void* __restrict__ w,
-                                                           uint8_t* __restrict__ wpack,
-                                                           int* err, int O, int C, int T,
-                                                           int Cg, int CBg, int numKB,
-                                                           int nrows, int cchunks, int half_mma,
-                                                           int tap_pairs) {
+__device__ __forceinline__ void pack_weights_body(const void* __restrict__ w,
+                                                  uint8_t* __restrict__ wpack, int* err, int O,
+                                                  int C, int T, int Cg, int CBg, int numKB,
+                                                  int nrows, int cchunks, int half_mma,
+                                                  int tap_pairs, int blk, int nblk) {
   using TR = PrecTraits<PREC>;
   constexpr int EPC = TR::kChunkElems, KC = TR::kBlockElems;
-  if (blockIdx.x == 0 && threadIdx.x == 0) *err = 0;
+  if (blk == 0 && threadIdx.x == 0) *err = 0;
   const size_t total = static_cast<size_t>(cchunks) * numKB * nrows * 8;
-  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+  for (size_t idx = blk * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(nblk) * blockDim.x) {
     const int jc = static_cast<int>(idx & 7);
     const int row = static_cast<int>((idx >> 3) % nrows);
     const size_t blk = (idx >> 3) / nrows;  // cc * numKB + kb
@@ -1342,6 +1343,60 @@ __global__ void __launch_bounds__(256) pack_weights_kernel(const void* __restric
     *reinterpret_cast<uint4*>(wpack + dst) = hi;
     if (TR::kNumBTiles == 2)
       *reinterpret_cast<uint4*>(wpack + dst + static_cast<size_t>(nrows) * kRowBytes) = lo;
+  }
+}
+template <int PREC>
+__global__ void __launch_bounds__(256) pack_weights_kernel(const void* __restrict__ w,
+                                                           uint8_t* __restrict__ wpack,
+                                                           int* err, int O, int C, int T,
+                                                           int Cg, int CBg, int numKB,
+                                                           int nrows, int cchunks, int half_mma,
+                                                           int tap_pairs) {
+  pack_weights_body<PREC>(w, wpack, err, O, C, T, Cg, CBg, numKB, nrows, cchunks, half_mma,
+                          tap_pairs, blockIdx.x, gridDim.x);
+}
+
+// ------------------------------------------------------------------ the two pre-passes, one launch
+// Blocks [0, tr_blocks) transpose x to channels-last (tiled kernels where channel and pixel
+// counts allow, the generic tile otherwise), the remaining blocks pack the weights into B tiles
+// (and clear the error word). The two are independent, so the packing's latency hides under the
+// transpose instead of adding a launch after it.
+struct PrepassArgs {
+  const void* x;
+  void* xt;
+  int C, HW, tiled;            // tiled: the fp16 / int8 tiled transpose
+  int tiles_x, tiles_y, tr_blocks;
+  const void* w;
+  uint8_t* wpack;
+  int* err;
+  int O, T, Cg, CBg, numKB, nrows, cchunks, half_mma, tap_pairs;
+};
+
+template <int PREC>
+__global__ void __launch_bounds__(256) prepass_kernel(const PrepassArgs a) {
+  using XT = typename PrecTraits<PREC>::X;
+  const int b = static_cast<int>(blockIdx.x);
+  if (b < a.tr_blocks) {
+    const int bx = b % a.tiles_x, r = b / a.tiles_x;
+    const int by = r % a.tiles_y, n = r / a.tiles_y;
+    if constexpr (PREC == PREC_F16) {
+      if (a.tiled) {
+        transpose_f16_tile(static_cast<const __half*>(a.x), static_cast<__half*>(a.xt), a.C, a.HW,
+                           bx, by, n);
+        return;
+      }
+    } else if constexpr (PREC == PREC_I8) {
+      if (a.tiled) {
+        transpose_i8_tile(static_cast<const int8_t*>(a.x), static_cast<int8_t*>(a.xt), a.C, a.HW,
+                          bx, by, n);
+        return;
+      }
+    }
+    transpose_tile<XT>(static_cast<const XT*>(a.x), static_cast<XT*>(a.xt), a.C, a.HW, bx, by, n);
+  } else {
+    pack_weights_body<PREC>(a.w, a.wpack, a.err, a.O, a.C, a.T, a.Cg, a.CBg, a.numKB, a.nrows,
+                            a.cchunks, a.half_mma, a.tap_pairs, b - a.tr_blocks,
+                            static_cast<int>(gridDim.x) - a.tr_blocks);
   }
 }
 

@@ -124,7 +124,7 @@ def test_workspace_rule():
     w_bytes = 9 * 4 * 256 * 128  # 36 K-blocks x 256 rows x 128 B
     assert x_bytes + w_bytes <= ws <= x_bytes + w_bytes + 4096
     assert capi.uses_tensor_cores(d)
-    assert capi.launch_count(d) == 3
+    assert capi.launch_count(d) == 2  # one pre-pass launch (transpose + packing), main kernel
     # scales with N (the reference's rule ignored N)
     d1 = capi.make_desc(1, 256, 64, 64, 256, dtype=DType.HALF)
     assert capi.workspace_size(d1) < ws
