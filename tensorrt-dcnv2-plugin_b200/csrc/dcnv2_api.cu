@@ -470,8 +470,9 @@ dcnv2_status launch_head(const HeadLaunch& h, DevInfo* di, const void* x_nhwc, c
                               cuuint64_t(a.N)};
   const cuuint64_t strides[3] = {cuuint64_t(a.C) * 2, cuuint64_t(a.W) * a.C * 2,
                                  cuuint64_t(a.H) * a.W * a.C * 2};
+  const cuuint32_t rows = static_cast<cuuint32_t>(a.win_mode ? a.TR + a.K - 1 : a.TR);
   const cuuint32_t box[4] = {static_cast<cuuint32_t>(kRowBytes), static_cast<cuuint32_t>(a.TW),
-                             static_cast<cuuint32_t>(a.TR), 1u};
+                             rows, 1u};
   const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
   CUtensorMap tmap;
   std::memset(&tmap, 0, sizeof(tmap));
@@ -909,24 +910,42 @@ dcnv2_status make_head_plan(const dcnv2_desc* d, HeadPlan* hp) {
   a.n_mma = static_cast<int>(cdiv(n_head, 16) * 16);
   hp->h.cb = static_cast<int>(cdiv(p.C, 64));
   a.numKB = hp->h.cb * p.T;
-  int tw = 1;
-  while (tw < p.W && tw < kTileM) tw <<= 1;
-  a.TW = tw;
-  a.TR = kTileM / tw;
+  // Window mode where the tile's columns are a multiple of 8 and two stages (a channel block's
+  // K windows + its K*K weight tiles each) fit: tiles of 8 x 16 pixels (16 x 8 below 16 columns);
+  // otherwise one box per tap with the tile as wide as the image (up to 128 columns).
+  const size_t fixed = 1024 + 256;  // alignment slack, barriers
+  a.b_stage_bytes = static_cast<uint32_t>(a.n_mma) * kRowBytes;
+  if (p.W >= 8) {
+    const int tw = p.W >= 16 ? 16 : 8, tr = kTileM / tw;
+    const uint32_t wb = static_cast<uint32_t>((tr + p.K - 1) * tw) * kRowBytes;
+    const size_t stage = size_t(p.K) * wb + size_t(p.T) * a.b_stage_bytes;
+    if (2 * stage + fixed <= kSmemLimit) {
+      a.win_mode = 1;
+      a.TW = tw;
+      a.TR = tr;
+      a.win_bytes = wb;
+      a.stages = 2;
+      hp->h.smem = fixed + 2 * stage;
+    }
+  }
+  if (!a.win_mode) {
+    int tw = 1;
+    while (tw < p.W && tw < kTileM) tw <<= 1;
+    a.TW = tw;
+    a.TR = kTileM / tw;
+    int stages = static_cast<int>((kSmemLimit - fixed) / (kHeadABytes + a.b_stage_bytes));
+    a.stages = stages > kHeadMaxStages ? kHeadMaxStages : stages;
+    hp->h.smem = fixed + size_t(a.stages) * (kHeadABytes + a.b_stage_bytes);
+  }
   a.tiles_x = static_cast<int>(cdiv(p.W, a.TW));
   a.tiles_y = static_cast<int>(cdiv(p.H, a.TR));
   const int64_t tiles = int64_t(p.N) * a.tiles_x * a.tiles_y;
   if (tiles >= (int64_t(1) << 31)) return DCNV2_ERR_INVALID_ARG;
   a.num_tiles = static_cast<int>(tiles);
-  a.b_stage_bytes = static_cast<uint32_t>(a.n_mma) * kRowBytes;
   uint32_t cols = 32;
   while (cols < static_cast<uint32_t>(2 * a.n_mma)) cols <<= 1;
   a.tmem_cols = cols;
-  const size_t fixed = 1024 + 256;  // alignment slack, barriers
-  int stages = static_cast<int>((kSmemLimit - fixed) / (kHeadABytes + a.b_stage_bytes));
-  a.stages = stages > kHeadMaxStages ? kHeadMaxStages : stages;
   a.timeout_ns = kDefaultTimeoutNs;
-  hp->h.smem = fixed + size_t(a.stages) * (kHeadABytes + a.b_stage_bytes);
   const size_t plane = size_t(p.H) * p.W;
   size_t off = align_up(p.ws_bytes, 1024);
   hp->off_hw = off;

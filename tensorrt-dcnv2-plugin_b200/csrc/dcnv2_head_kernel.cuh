@@ -15,6 +15,13 @@
 // in shared memory exactly as the MMA descriptor reads it, and the box's out-of-image part reads
 // zeros, which is the convolution's zero padding. No sampler threads are involved.
 //
+// Window mode (TW a multiple of 8 and two stages fit): a stage is one channel block — K TMA
+// boxes of (TR + K - 1) rows x TW columns, box kj shifted by the tap column kj, plus one bulk copy
+// of the block's K*K weight tiles. The A tile of tap (ki, kj) is rows [ki*TW, ki*TW + 128) of box
+// kj: it starts on a 1024-byte swizzle atom (TW*128 is a multiple of 1024), so the same
+// descriptor reads it. Per channel block that is K*(TR+K-1)*TW line requests instead of
+// K*K*TR*TW (3x3, 8 x 16 tiles: 480 instead of 1152).
+//
 // Roles (192 threads): warp 0 producer (TMA box of A + bulk copy of B per K-block into a ring of
 // stages), warp 1 MMA issuer (tcgen05.mma kind::f16, fp32 accumulators in TMEM, two of them so
 // that the epilogue of a tile overlaps the next tile), warps 2-5 epilogue (tcgen05.ld, + bias,
@@ -41,7 +48,9 @@ struct HeadArgs {
   int TW, TR;             // tile: TR rows x TW columns, TR * TW = 128
   int tiles_x, tiles_y, num_tiles;
   int stages;
-  uint32_t b_stage_bytes, tmem_cols;
+  uint32_t b_stage_bytes, tmem_cols;  // b_stage_bytes: one K-block's weight tile
+  int win_mode;                        // 1: a stage holds a channel block's K windows + T tiles
+  uint32_t win_bytes;                  // window mode: one box, (TR + K - 1) * TW * 128 bytes
   unsigned long long timeout_ns;
 };
 
@@ -61,10 +70,16 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = args.stages;
-  // [S A stages (16 KB, 1 KB aligned) | S B stages | barriers]
+  // [S A stages (1 KB aligned) | S B stages | barriers]; per stage A is one 16 KB box (tap mode)
+  // or K windows (window mode), B one weight tile (tap mode) or the T tiles of a channel block
+  const uint32_t a_bytes = args.win_mode ? static_cast<uint32_t>(args.K) * args.win_bytes
+                                         : kHeadABytes;
+  const uint32_t b_bytes = args.win_mode ? static_cast<uint32_t>(args.T) * args.b_stage_bytes
+                                         : args.b_stage_bytes;
+  const int n_steps = args.win_mode ? args.numKB / args.T : args.numKB;  // stages per tile
   uint8_t* a_smem = smem;
-  uint8_t* b_smem = smem + static_cast<size_t>(S) * kHeadABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(b_smem + static_cast<size_t>(S) * args.b_stage_bytes);
+  uint8_t* b_smem = smem + static_cast<size_t>(S) * a_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(b_smem + static_cast<size_t>(S) * b_bytes);
   const uint32_t full = ptx::smem_addr(bars);     // [S] A and B of a stage landed
   const uint32_t empty = full + 8 * S;            // [S] MMAs of a stage done
   const uint32_t tfull = empty + 8 * S;           // [2] accumulator ready
@@ -106,20 +121,31 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
       for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
         int img, oy0, ox0;
         head_tile(args, tile, img, oy0, ox0);
-        for (int kb = 0; kb < args.numKB; ++kb, ++it) {
+        for (int step = 0; step < n_steps; ++step, ++it) {
           if (!wait_bar<kSuspend>(empty + 8 * s, ph ^ 1u, wc, DCNV2_DEVERR_TIMEOUT_PRODUCER)) {
             ok = false;
             break;
           }
-          const int t = kb % args.T, cb = kb / args.T;
-          const int ki = t / args.K, kj = t - ki * args.K;
-          ptx::mbar_arrive_expect_tx(full + 8 * s, kHeadABytes + args.b_stage_bytes);
-          // channel block cb (128 bytes, 16-byte aligned), columns and rows shifted by the tap
-          ptx::tma_load_4d(a_base + s * kHeadABytes, &tmap_x, cb * kRowBytes, ox0 + kj - args.pad,
-                           oy0 + ki - args.pad, img, full + 8 * s);
-          ptx::bulk_copy_g2s(b_base + s * args.b_stage_bytes,
-                             args.wpack + static_cast<size_t>(kb) * args.b_stage_bytes,
-                             args.b_stage_bytes, full + 8 * s);
+          ptx::mbar_arrive_expect_tx(full + 8 * s, a_bytes + b_bytes);
+          if (args.win_mode) {
+            // channel block `step`: K windows, box kj shifted by the tap column kj
+            for (int kj = 0; kj < args.K; ++kj)
+              ptx::tma_load_4d(a_base + s * a_bytes + kj * args.win_bytes, &tmap_x,
+                               step * kRowBytes, ox0 + kj - args.pad, oy0 - args.pad, img,
+                               full + 8 * s);
+            ptx::bulk_copy_g2s(b_base + s * b_bytes,
+                               args.wpack + static_cast<size_t>(step) * b_bytes, b_bytes,
+                               full + 8 * s);
+          } else {
+            const int kb = step, t = kb % args.T, cb = kb / args.T;
+            const int ki = t / args.K, kj = t - ki * args.K;
+            // channel block cb (128 bytes, 16-byte aligned), columns and rows shifted by the tap
+            ptx::tma_load_4d(a_base + s * a_bytes, &tmap_x, cb * kRowBytes, ox0 + kj - args.pad,
+                             oy0 + ki - args.pad, img, full + 8 * s);
+            ptx::bulk_copy_g2s(b_base + s * b_bytes,
+                               args.wpack + static_cast<size_t>(kb) * b_bytes, b_bytes,
+                               full + 8 * s);
+          }
           if (++s == S) { s = 0; ph ^= 1u; }
         }
       }
@@ -146,17 +172,28 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
         }
         ptx::tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * args.n_mma);
-        for (int kb = 0; kb < args.numKB; ++kb) {
+        for (int step = 0; step < n_steps; ++step) {
           if (!wait_bar(full + 8 * s, ph, wc, DCNV2_DEVERR_TIMEOUT_MMA)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          const uint64_t ad = desc0 | (((a_base + s * kHeadABytes) >> 4) & 0x3FFFu);
-          const uint64_t bd = desc0 | (((b_base + s * args.b_stage_bytes) >> 4) & 0x3FFFu);
+          const int taps = args.win_mode ? args.T : 1;
+          for (int t = 0; t < taps; ++t) {
+            // window mode: tap (ki, kj) reads rows [ki*TW, ki*TW + 128) of window kj
+            const int ki = t / args.K, kj = t - ki * args.K;
+            const uint32_t a_addr = a_base + s * a_bytes +
+                                    (args.win_mode ? kj * args.win_bytes +
+                                                         static_cast<uint32_t>(ki * args.TW) * kRowBytes
+                                                   : 0u);
+            const uint32_t b_addr = b_base + s * b_bytes + t * args.b_stage_bytes;
+            const uint64_t ad = desc0 | ((a_addr >> 4) & 0x3FFFu);
+            const uint64_t bd = desc0 | ((b_addr >> 4) & 0x3FFFu);
 #pragma unroll
-          for (int k = 0; k < 4; ++k)  // K-step k: 32 bytes further along the rows
-            ptx::mma_f16(d, ad + 2 * k, bd + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < 4; ++k)  // K-step k: 32 bytes further along the rows
+              ptx::mma_f16(d, ad + 2 * k, bd + 2 * k, idesc,
+                           (step > 0 || t > 0 || k > 0) ? 1u : 0u);
+          }
           ptx::tc_commit(empty + 8 * s);
           if (++s == S) { s = 0; ph ^= 1u; }
         }
