@@ -221,3 +221,33 @@ def test_forward_with_head_support_rules():
         assert capi.forward_with_head_workspace_size(bad) == 0
     assert capi.forward_with_head_workspace_size(
         capi.make_desc(1, 256, 64, 64, 256, 3, 1, 1, 1, 8, DType.HALF)) > 0
+
+
+def test_kernel_override_validation_and_plan_effect():
+    """The measurement override changes the planned kernel and rejects out-of-range values; the
+    automatic selection picks CTA pairs only for the A-in-shared-memory kernel above 256 output
+    channels (the plan is visible through the kernel name and the workspace size)."""
+    d = capi.make_desc(2, 256, 32, 32, 256, dtype=DType.HALF)
+    try:
+        assert capi.main_kernel(d) == "dcnv2_fused_ta_kernel"
+        capi.set_kernel_override(capi.Kernel.SMEM)
+        assert capi.main_kernel(d) == "dcnv2_fused_kernel"
+        capi.set_kernel_override(capi.Kernel.TA, capi.Pair.PAIRS)
+        assert capi.main_kernel(d) == "dcnv2_fused_ta_kernel"
+        for bad in ((3, 0), (-1, 0), (0, 3), (0, -1)):
+            assert capi.lib.dcnv2_diag_set_kernel_override(*bad) == Status.ERR_INVALID_ARG
+    finally:
+        capi.set_kernel_override(capi.Kernel.AUTO, capi.Pair.AUTO)
+    assert capi.main_kernel(d) == "dcnv2_fused_ta_kernel"
+    wide = capi.make_desc(1, 512, 16, 16, 512, 3, 1, 2, 2, 8, DType.INT8)
+    assert capi.main_kernel(wide) == "dcnv2_fused_kernel"
+
+
+def test_binary_arch_without_device():
+    """Without a usable sm_100 device the architecture query reports no device instead of
+    failing."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present (the GPU test covers the query)")
+    v = ctypes.c_int32(0)
+    assert capi.lib.dcnv2_diag_binary_arch(ctypes.byref(v)) == Status.ERR_NO_DEVICE
