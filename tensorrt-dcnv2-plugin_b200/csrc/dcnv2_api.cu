@@ -184,10 +184,8 @@ void plan_ta(Plan* pl) {
   p.a_stages = p.prec == PREC_F16 ? TaLayout<PREC_F16>::kAStages : TaLayout<PREC_I8>::kAStages;
   p.a_stage_bytes = 0;
   p.b_kb_bytes = size_t(p.nrows) * kRowBytes;
-  p.b_stage_bytes = static_cast<uint32_t>(p.b_kb_bytes / (p.pair ? 2 : 1));
-  const int64_t cta_tiles_per_img = cdiv(int64_t(p.Ho) * p.Wo, kTileM);
-  p.tiles_per_img = static_cast<int>(p.pair ? cdiv(int64_t(p.Ho) * p.Wo, 2 * kTileM)
-                                            : cta_tiles_per_img);
+  p.b_stage_bytes = static_cast<uint32_t>(p.b_kb_bytes);
+  p.tiles_per_img = static_cast<int>(cdiv(int64_t(p.Ho) * p.Wo, kTileM));
   p.num_tiles = static_cast<int>(int64_t(p.N) * p.tiles_per_img * p.cchunks);
   const size_t fixed = 1024 + 512 + 1024;  // alignment slack, barriers, staged bias (fp32)
   const size_t per_stage = p.b_stage_bytes;
@@ -300,11 +298,13 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
     uint32_t cols = 32;
     while (cols < static_cast<uint32_t>(p.acc_bufs * p.nrows)) cols <<= 1;
     p.tmem_cols = cols;
-    // fp16 / int8 run as CTA pairs (M = 256 per MMA, each CTA holding half of B) when a tile
-    // carries more than 256 output channels: each CTA then copies half of the 512-row weight
-    // tile per K-block, and four stages fit instead of two (512-channel dg8 layer: fp16
-    // 2.29 -> 2.20 ms, int8 2.31 -> 1.99 ms). Up to 256 channels one CTA per tile measured faster
-    // (the pair adds a cross-CTA hand-off to every K-block). The override forces either.
+    // fp16 / int8 tiles of this kernel run as CTA pairs (M = 256 per MMA, each CTA holding half
+    // of B) when they carry more than 256 output channels: each CTA then copies half of the
+    // 512-row weight tile per K-block, and four stages fit instead of two (512-channel dg8
+    // layer: fp16 2.29 -> 2.20 ms, int8 2.31 -> 1.99 ms). Up to 256 channels one CTA per tile
+    // measured faster (the pair adds a cross-CTA hand-off to every K-block); the TMEM-A kernel,
+    // which takes those layers, has no pair variant (measured 0.43-0.46 against 0.35 ms). The
+    // override forces either here.
     const int pov = g_pair_override.load();
     p.pair = (prec == PREC_F16 || prec == PREC_I8) &&
              (pov == POV_PAIRS || (pov == POV_AUTO && p.nsub >= 2));
@@ -372,7 +372,7 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
     const bool force_ta = kov == KOV_TA;
     if (!force_smem && (p.O <= 256 || force_ta)) {
       Plan t = p;
-      t.pair = g_pair_override.load() == POV_PAIRS;  // the TMEM-A kernel pairs only when forced
+      t.pair = false;  // the TMEM-A kernel runs one CTA per tile
       plan_ta(&t);
       if (t.ta) p = t;
     }
@@ -507,19 +507,13 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
            set_smem_attr(dcnv2_fused_kernel<PREC, true, 0, false>) &&
            set_smem_attr(dcnv2_fused_kernel<PREC, true, 9, true>) &&
            set_smem_attr(dcnv2_fused_kernel<PREC, true, 0, true>) &&
-           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 9, false>) &&
-           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 9, true>) &&
-           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, false>) &&
-           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, true>) &&
-           set_smem_attr(dcnv2_fused_ta_kernel<PREC, true, 0, false>) &&
-           set_smem_attr(dcnv2_fused_ta_kernel<PREC, true, 0, true>) &&
-           set_smem_attr(dcnv2_fused_ta_kernel<PREC, true, 9, false>) &&
-           set_smem_attr(dcnv2_fused_ta_kernel<PREC, true, 9, true>);
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 9>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, true, 0>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, true, 9>);
     if constexpr (PREC == PREC_I8)
-      ok = ok && set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, false>) &&
-           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0, true>) &&
-           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 9, false>) &&
-           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 9, true>);
+      ok = ok && set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 0>) &&
+           set_smem_attr(dcnv2_fused_ta_kernel<PREC, false, 9>);
     if (!ok) return DCNV2_ERR_CUDA;
     di->attr_set.fetch_or(bit, std::memory_order_acq_rel);
   }
@@ -616,32 +610,16 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
     if (p.ta) {
       FusedFn kfn;
       if constexpr (PREC == PREC_F16) {
-        if (p.precise && k3) kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, true, 9, true>
-                                          : dcnv2_fused_ta_kernel<PREC, true, 9, false>;
-        else if (p.precise) kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, true, 0, true>
-                                         : dcnv2_fused_ta_kernel<PREC, true, 0, false>;
-        else if (k3) kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, false, 9, true>
-                                  : dcnv2_fused_ta_kernel<PREC, false, 9, false>;
-        else kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, false, 0, true>
-                          : dcnv2_fused_ta_kernel<PREC, false, 0, false>;
-      } else if (k3) {
-        kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, false, 9, true>
-                     : dcnv2_fused_ta_kernel<PREC, false, 9, false>;
+        if (p.precise && k3) kfn = dcnv2_fused_ta_kernel<PREC, true, 9>;
+        else if (p.precise) kfn = dcnv2_fused_ta_kernel<PREC, true, 0>;
+        else if (k3) kfn = dcnv2_fused_ta_kernel<PREC, false, 9>;
+        else kfn = dcnv2_fused_ta_kernel<PREC, false, 0>;
       } else {
-        kfn = p.pair ? dcnv2_fused_ta_kernel<PREC, false, 0, true>
-                     : dcnv2_fused_ta_kernel<PREC, false, 0, false>;
+        kfn = k3 ? dcnv2_fused_ta_kernel<PREC, false, 9> : dcnv2_fused_ta_kernel<PREC, false, 0>;
       }
-      if (p.pair) {
-        const int nc = (p.num_tiles < di->sm_count / 2) ? p.num_tiles : di->sm_count / 2;
-        cudaLaunchAttribute at[1];
-        cudaLaunchConfig_t cfg = pair_launch_config(2 * nc, p.smem_bytes, st, at);
-        cfg.blockDim = dim3(kTaThreads, 1, 1);
-        e = cudaLaunchKernelEx(&cfg, kfn, a, tmap);
-      } else {
-        const int grid = p.num_tiles < di->sm_count ? p.num_tiles : di->sm_count;
-        kfn<<<grid, kTaThreads, p.smem_bytes, st>>>(a, tmap);
-        e = cudaGetLastError();
-      }
+      const int grid = p.num_tiles < di->sm_count ? p.num_tiles : di->sm_count;
+      kfn<<<grid, kTaThreads, p.smem_bytes, st>>>(a, tmap);
+      e = cudaGetLastError();
       mk.mark(st);
       return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
     }
@@ -1078,7 +1056,7 @@ dcnv2_status dcnv2_diag_set_kernel_override(int32_t kernel, int32_t pair) {
 dcnv2_status dcnv2_diag_binary_arch(int32_t* binary_version) {
   if (!binary_version) return DCNV2_ERR_INVALID_ARG;
   cudaFuncAttributes fa;
-  if (cudaFuncGetAttributes(&fa, dcnv2_fused_ta_kernel<PREC_F16, false, 9, false>) != cudaSuccess) {
+  if (cudaFuncGetAttributes(&fa, dcnv2_fused_ta_kernel<PREC_F16, false, 9>) != cudaSuccess) {
     cudaGetLastError();
     return DCNV2_ERR_NO_DEVICE;
   }

@@ -50,7 +50,7 @@ constexpr int kTaThreads = (kSampWarp0 + kTaSampWarps) * 32;  // 576: 18 warps, 
 
 struct TaMmaParams {
   uint32_t b_base, b_stage_bytes, tmem_base;
-  uint32_t a_full, a_empty, b_full, b_empty, peer_full, tfull, tempty, drain;
+  uint32_t a_full, a_empty, b_full, b_empty, tfull, tempty, drain;
   int SA, SB, num_tiles, tile0, tstep, numKB, n_mma;
   WaitCtx wc;
 };
@@ -60,9 +60,9 @@ struct TaMmaParams {
 // that each stage is released as soon as the MMAs reading it complete. One accumulator: a tile
 // starts after the epilogue has read the previous one; the A ring keeps the samplers busy
 // meanwhile.
-template <int PREC, bool PAIR>
+template <int PREC>
 __device__ __noinline__ void ta_mma_issuer(const TaMmaParams mp) {
-  const uint32_t m = PAIR ? 2 * kTileM : kTileM;
+  const uint32_t m = kTileM;
   const uint32_t idesc = PREC == PREC_F16 ? ptx::make_idesc(1, 0, mp.n_mma, m)
                                           : ptx::make_idesc(2, 1, mp.n_mma, m);
   const uint64_t desc0 = ptx::sw128_kmajor_desc(0);
@@ -72,10 +72,8 @@ __device__ __noinline__ void ta_mma_issuer(const TaMmaParams mp) {
   uint32_t pa = 0, pb = 0, use = 0;
   bool ok = true;
   for (int tile = mp.tile0; tile < mp.num_tiles && ok; tile += mp.tstep) {
-    // the accumulator drained: a suspended wait wakes when the phase completes (the CTA pair's
-    // leader polls its cluster-scope barrier)
-    if (!(PAIR ? wait_bar<64, true>(mp.tempty, use ^ 1u, wc, DCNV2_DEVERR_TIMEOUT_MMA)
-               : wait_bar<kSuspend>(mp.tempty, use ^ 1u, wc, DCNV2_DEVERR_TIMEOUT_MMA))) {
+    // the accumulator drained: a suspended wait wakes when the phase completes
+    if (!wait_bar<kSuspend>(mp.tempty, use ^ 1u, wc, DCNV2_DEVERR_TIMEOUT_MMA)) {
       ok = false;
       break;
     }
@@ -86,8 +84,7 @@ __device__ __noinline__ void ta_mma_issuer(const TaMmaParams mp) {
     for (int kb = 0; kb < mp.numKB; ++kb) {
       if (!ready) {
         if (!wait_bar(mp.b_full + 8 * sb, pb, wc, DCNV2_DEVERR_TIMEOUT_MMA) ||
-            !wait_bar(mp.a_full + 8 * sa, pa, wc, DCNV2_DEVERR_TIMEOUT_MMA) ||
-            (PAIR && !wait_bar<0, true>(mp.peer_full + 8 * sa, pa, wc, DCNV2_DEVERR_TIMEOUT_MMA))) {
+            !wait_bar(mp.a_full + 8 * sa, pa, wc, DCNV2_DEVERR_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
@@ -102,37 +99,24 @@ __device__ __noinline__ void ta_mma_issuer(const TaMmaParams mp) {
       if (kb + 1 < mp.numKB) {
         nxt = ptx::mbar_test_wait(mp.b_full + 8 * sb1, pb1) &
               ptx::mbar_test_wait(mp.a_full + 8 * sa1, pa1);
-        if (PAIR) nxt &= ptx::mbar_test_wait_cluster(mp.peer_full + 8 * sa1, pa1);
       }
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         // K-step k: 8 TMEM columns of A, 32 bytes further along the B rows
         const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
-        if (PAIR) {
-          if (PREC == PREC_F16) ptx::mma_f16_ta_pair(mp.tmem_base, at + 8 * k, bd0 + 2 * k, idesc, accum);
-          else ptx::mma_i8_ta_pair(mp.tmem_base, at + 8 * k, bd0 + 2 * k, idesc, accum);
-        } else {
-          if (PREC == PREC_F16) ptx::mma_f16_ta(mp.tmem_base, at + 8 * k, bd0 + 2 * k, idesc, accum);
-          else ptx::mma_i8_ta(mp.tmem_base, at + 8 * k, bd0 + 2 * k, idesc, accum);
-        }
+        if (PREC == PREC_F16) ptx::mma_f16_ta(mp.tmem_base, at + 8 * k, bd0 + 2 * k, idesc, accum);
+        else ptx::mma_i8_ta(mp.tmem_base, at + 8 * k, bd0 + 2 * k, idesc, accum);
       }
-      if (PAIR) {
-        ptx::tc_commit_pair(mp.a_empty + 8 * sa, 3);
-        ptx::tc_commit_pair(mp.b_empty + 8 * sb, 3);
-      } else {
-        ptx::tc_commit(mp.a_empty + 8 * sa);
-        ptx::tc_commit(mp.b_empty + 8 * sb);
-      }
+      ptx::tc_commit(mp.a_empty + 8 * sa);
+      ptx::tc_commit(mp.b_empty + 8 * sb);
       sa = sa1; sb = sb1; pa = pa1; pb = pb1;
       ready = nxt != 0;
     }
     if (!ok) break;
-    if (PAIR) ptx::tc_commit_pair(mp.tfull, 3);
-    else ptx::tc_commit(mp.tfull);
+    ptx::tc_commit(mp.tfull);
     use ^= 1u;
   }
-  if (PAIR) ptx::tc_commit_pair(mp.drain, 3);
-  else ptx::tc_commit(mp.drain);
+  ptx::tc_commit(mp.drain);
   wait_bar(mp.drain, 0, wc, DCNV2_DEVERR_TIMEOUT_DRAIN);
 }
 
@@ -190,7 +174,7 @@ __device__ __forceinline__ void unrotate_chunks(uint32_t (&o)[32], int r) {
   xchg_slots<2>(o, r & 4);
 }
 
-template <int PREC, bool PRECISE, int KT, bool PAIR>
+template <int PREC, bool PRECISE, int KT>
 __global__ void __launch_bounds__(kTaThreads, 1)
     dcnv2_fused_ta_kernel(const FusedArgs args, const __grid_constant__ CUtensorMap tmap_x) {
   using TR = PrecTraits<PREC>;
@@ -208,14 +192,13 @@ __global__ void __launch_bounds__(kTaThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(b_smem + static_cast<size_t>(SB) * args.b_stage_bytes);
   const uint32_t a_full = ptx::smem_addr(bars);   // [SA] sampler warps -> MMA
   const uint32_t a_empty = a_full + 8 * SA;       // [SA] MMA commit -> samplers
-  const uint32_t peer_full = a_empty + 8 * SA;    // [SA] pair leader: stage full in rank 1
-  const uint32_t b_full = peer_full + 8 * SA;     // [SB] weight copy landed
+  const uint32_t b_full = a_empty + 8 * SA;       // [SB] weight copy landed
   const uint32_t b_empty = b_full + 8 * SB;       // [SB] MMA commit -> producer
   const uint32_t tfull = b_empty + 8 * SB;        // accumulator ready
   const uint32_t tempty = tfull + 8;              // accumulator read by the epilogue(s)
   const uint32_t drain = tempty + 8;
   const uint32_t win_full = drain + 8;            // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * SA + 2 * SB + 7);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * SA + 2 * SB + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // [2] sampler warps done with window buffer b, counted over the kernel (the warp that
   // completes a use loads the buffer's next window), and the number of windows issued
@@ -224,23 +207,21 @@ __global__ void __launch_bounds__(kTaThreads, 1)
   // bias of the (single) output-channel chunk as fp32, after the 512 bytes of barriers
   float* bias_smem = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 512);
   const WaitCtx wc{args.timeout_ns, args.err, abort_flag};
-  const int rank = PAIR ? static_cast<int>(ptx::cluster_ctarank()) : 0;
-  const int tile0 = PAIR ? static_cast<int>(ptx::cluster_id_x()) : static_cast<int>(blockIdx.x);
-  const int tstep = PAIR ? static_cast<int>(ptx::num_clusters_x()) : static_cast<int>(gridDim.x);
-  auto pix_base = [&](int pt) { return pt * (PAIR ? 2 * kTileM : kTileM) + rank * kTileM; };
+  const int tile0 = static_cast<int>(blockIdx.x);
+  const int tstep = static_cast<int>(gridDim.x);
+  auto pix_base = [&](int pt) { return pt * kTileM; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SA; ++s) {
       ptx::mbar_init(a_full + 8 * s, 4);  // one sampler warp per lane quadrant
       ptx::mbar_init(a_empty + 8 * s, 1);
-      ptx::mbar_init(peer_full + 8 * s, 1);
     }
     for (int s = 0; s < SB; ++s) {
       ptx::mbar_init(b_full + 8 * s, 1);
       ptx::mbar_init(b_empty + 8 * s, 1);
     }
     ptx::mbar_init(tfull, 1);
-    ptx::mbar_init(tempty, PAIR ? 2 * kNumEpiWarps : kNumEpiWarps);
+    ptx::mbar_init(tempty, kNumEpiWarps);
     ptx::mbar_init(drain, 1);
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(win_full + 8 * i, 1);
@@ -260,17 +241,11 @@ __global__ void __launch_bounds__(kTaThreads, 1)
     }
   }
   if (warp == kMmaWarp) {
-    if (PAIR) {
-      ptx::tmem_alloc_pair(ptx::smem_addr(tmem_slot), kTaTmemCols);
-      ptx::tmem_relinquish_pair();
-    } else {
-      ptx::tmem_alloc(ptx::smem_addr(tmem_slot), kTaTmemCols);
-      ptx::tmem_relinquish();
-    }
+    ptx::tmem_alloc(ptx::smem_addr(tmem_slot), kTaTmemCols);
+    ptx::tmem_relinquish();
   }
   ptx::tc_fence_before();
-  if (PAIR) ptx::cluster_sync();
-  else __syncthreads();
+  __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -281,12 +256,11 @@ __global__ void __launch_bounds__(kTaThreads, 1)
       uint32_t ph = 0;
       bool ok = true;
       const uint32_t b_base = ptx::smem_addr(b_smem);
-      const size_t kb_bytes = static_cast<size_t>(args.b_stage_bytes) * (PAIR ? 2 : 1);
+      const size_t kb_bytes = static_cast<size_t>(args.b_stage_bytes);
       for (int tile = tile0; tile < args.num_tiles && ok; tile += tstep) {
         int img, pt, cc;
         decode_tile(args, tile, img, pt, cc);
-        const uint8_t* src = args.wpack + static_cast<size_t>(cc) * args.numKB * kb_bytes +
-                             static_cast<size_t>(rank) * args.b_stage_bytes;
+        const uint8_t* src = args.wpack + static_cast<size_t>(cc) * args.numKB * kb_bytes;
         for (int kb = 0; kb < args.numKB; ++kb, ++it) {
           if (!wait_bar<kSuspend>(b_empty + 8 * s, ph ^ 1, wc, DCNV2_DEVERR_TIMEOUT_PRODUCER)) {
             ok = false;
@@ -308,39 +282,17 @@ __global__ void __launch_bounds__(kTaThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && (!PAIR || rank == 0)) {
+    if (lane == 0) {
       TaMmaParams mp;
       mp.b_base = ptx::smem_addr(b_smem);
       mp.b_stage_bytes = args.b_stage_bytes;
       mp.tmem_base = tmem_base;
       mp.a_full = a_full; mp.a_empty = a_empty; mp.b_full = b_full; mp.b_empty = b_empty;
-      mp.peer_full = peer_full; mp.tfull = tfull; mp.tempty = tempty; mp.drain = drain;
+      mp.tfull = tfull; mp.tempty = tempty; mp.drain = drain;
       mp.SA = SA; mp.SB = SB; mp.num_tiles = args.num_tiles; mp.tile0 = tile0;
       mp.tstep = tstep; mp.numKB = args.numKB; mp.n_mma = args.n_mma;
       mp.wc = wc;
-      ta_mma_issuer<PREC, PAIR>(mp);
-    } else if (PAIR && rank != 0) {
-      // Rank 1 relay: once this CTA's A stage (TMEM) and B stage (smem) of a K-block are
-      // complete, tell the leader. The whole warp runs the loop (lane 0 arrives), so no lane of
-      // it waits at the kernel's final barrier meanwhile.
-      const uint32_t peer = ptx::mapa_shared(peer_full, 0);
-      int sa = 0, sb = 0;
-      uint32_t pa = 0, pb = 0;
-      bool ok = true;
-      for (int tile = tile0; tile < args.num_tiles && ok; tile += tstep) {
-        for (int kb = 0; kb < args.numKB; ++kb) {
-          const bool got = wait_bar<kSuspend>(a_full + 8 * sa, pa, wc, DCNV2_DEVERR_TIMEOUT_MMA) &&
-                           wait_bar<kSuspend>(b_full + 8 * sb, pb, wc, DCNV2_DEVERR_TIMEOUT_MMA);
-          if (!__all_sync(0xffffffffu, got)) {
-            ok = false;
-            break;
-          }
-          if (lane == 0) ptx::mbar_arrive_cluster(peer + 8 * sa);
-          if (++sa == SA) { sa = 0; pa ^= 1u; }
-          if (++sb == SB) { sb = 0; pb ^= 1u; }
-        }
-      }
-      wait_bar(drain, 0, wc, DCNV2_DEVERR_TIMEOUT_DRAIN);
+      ta_mma_issuer<PREC>(mp);
     }
   } else if (warp < kSampWarp0) {
     // ------------------------------------------------------------ epilogue
@@ -424,8 +376,7 @@ __global__ void __launch_bounds__(kTaThreads, 1)
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          if (PAIR && rank != 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(tempty, 0));
-          else ptx::mbar_arrive(tempty);
+          ptx::mbar_arrive(tempty);
         }
       };
       uint32_t ra[16], rb[16];
@@ -848,8 +799,7 @@ __global__ void __launch_bounds__(kTaThreads, 1)
   }
 
   ptx::tc_fence_before();
-  if (PAIR) ptx::cluster_sync();
-  else __syncthreads();
+  __syncthreads();
   if (args.use_win && warp == kSampWarp0 && lane == 0) {
     // window loads still in flight (after an early exit) land before shared memory is released
     const int issued = static_cast<int>(*reinterpret_cast<volatile uint32_t*>(win_issued));
@@ -860,8 +810,7 @@ __global__ void __launch_bounds__(kTaThreads, 1)
   if (warp == kMmaWarp) {
     __syncwarp();
     ptx::tc_fence_after();
-    if (PAIR) ptx::tmem_dealloc_pair(tmem_base, kTaTmemCols);
-    else ptx::tmem_dealloc(tmem_base, kTaTmemCols);
+    ptx::tmem_dealloc(tmem_base, kTaTmemCols);
   }
 }
 

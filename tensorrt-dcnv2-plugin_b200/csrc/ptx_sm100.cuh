@@ -255,9 +255,9 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_
       : "memory");
 }
 
-// A operand in tensor memory: D[tmem] (+)= A[tmem] * B[smem desc]^T. A row i sits in TMEM lane i
-// (lane i of the peer CTA for rows 128-255 of a pair), its K elements packed along consecutive
-// 32-bit columns from `a_tmem` (2 fp16 / 4 int8 per column).
+// A operand in tensor memory: D[tmem] (+)= A[tmem] * B[smem desc]^T. A row i sits in TMEM lane i,
+// its K elements packed along consecutive 32-bit columns from `a_tmem` (2 fp16 / 4 int8 per
+// column).
 __device__ __forceinline__ void mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
                                            uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -273,24 +273,6 @@ __device__ __forceinline__ void mma_i8_ta(uint32_t d_tmem, uint32_t a_tmem, uint
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_f16_ta_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                                uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_i8_ta_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                               uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::i8 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

@@ -311,18 +311,18 @@ def kernel_override():
 
 @pytest.mark.parametrize("shape", sorted(PAIR_SHAPES))
 def test_cta_pair_and_single_cta_paths_agree(shape, kernel_override):
-    """fp16 / int8 tiles run on one CTA (128 pixels) or on a CTA pair (cta_group::2, 256
-    pixels; automatic above 256 output channels in the shared-memory A kernel), forced here
-    both ways. Both meet the stated bounds and agree with each other."""
+    """The shared-memory A kernel runs fp16 / int8 tiles on one CTA (128 pixels) or on a CTA
+    pair (cta_group::2, 256 pixels; automatic above 256 output channels), forced here both ways.
+    Both meet the stated bounds and agree with each other."""
     fx = random_case(**PAIR_SHAPES[shape])
     h = half_inputs(fx)
     ref16 = oracle.forward_ref(h["x"], h["offset"], h["mask"], h["weight"], h["bias"],
                                *oattrs(fx), precision="fp16")
     xq, xs, wq, ws = quantized(fx)
-    kernel_override(capi.Kernel.AUTO, capi.Pair.PAIRS)
+    kernel_override(capi.Kernel.SMEM, capi.Pair.PAIRS)
     y16_pair = run_fp16(fx)
     y8_pair = run_int8(fx, xq, xs, wq, ws)
-    kernel_override(capi.Kernel.AUTO, capi.Pair.SINGLE)
+    kernel_override(capi.Kernel.SMEM, capi.Pair.SINGLE)
     y16_one = run_fp16(fx)
     y8_one = run_int8(fx, xq, xs, wq, ws)
     for y in (y16_pair, y16_one):
@@ -361,8 +361,9 @@ TA_SHAPES = {
 def test_tmem_a_kernel_matches_smem_a_kernel(shape, pair, kernel_override):
     """fp16 / int8 default to the kernel with the A operand in tensor memory (the "ta" override
     also forces it for > 256 output channels); the "smem" override selects the shared-memory A
-    kernel. Both meet the stated bounds against the oracle and agree with each other (same A
-    values, same K order)."""
+    kernel (here with CTA pairs forced on or off; the TMEM-A kernel always runs one CTA per tile).
+    Both meet the stated bounds against the oracle and agree with each other (same A values,
+    same K order)."""
     fx = random_case(**TA_SHAPES[shape])
     h = half_inputs(fx)
     ref16 = oracle.forward_ref(h["x"], h["offset"], h["mask"], h["weight"], h["bias"],
