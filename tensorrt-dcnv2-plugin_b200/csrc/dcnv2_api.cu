@@ -412,21 +412,25 @@ bool set_smem_attr(F* kfn) {
                               static_cast<int>(kSmemLimit)) == cudaSuccess;
 }
 
-// Launch configuration of a grid of CTA pairs (clusters of 2 along x). The cluster attribute is
-// written into the caller's `attr`, which must outlive the launch call.
-cudaLaunchConfig_t pair_launch_config(int grid, size_t smem, cudaStream_t st,
-                                      cudaLaunchAttribute (&attr)[1]) {
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+// Launch configuration of a main kernel: programmatic stream serialization (it may start while
+// the kernel ahead of it in the stream finishes, and calls griddep_wait before reading that
+// kernel's outputs) and, for `pair`, clusters of 2 CTAs along x. The attributes are written into
+// the caller's `attr`, which must outlive the launch call.
+cudaLaunchConfig_t main_launch_config(int grid, int threads, size_t smem, cudaStream_t st,
+                                      cudaLaunchAttribute (&attr)[2], bool pair) {
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pair ? 2 : 1;
   return cfg;
 }
 
@@ -483,8 +487,10 @@ dcnv2_status launch_head(const HeadLaunch& h, DevInfo* di, const void* x_nhwc, c
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return DCNV2_ERR_CUDA;
   mk.mark(st);
-  dcnv2_offset_head_kernel<<<h.grid, kHeadThreads, h.smem, st>>>(a, tmap);
-  return cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
+  cudaLaunchAttribute at[2];
+  const cudaLaunchConfig_t cfg = main_launch_config(h.grid, kHeadThreads, h.smem, st, at, false);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, dcnv2_offset_head_kernel, a, tmap);
+  return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
 }
 
 template <int PREC>
@@ -618,8 +624,10 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
         kfn = k3 ? dcnv2_fused_ta_kernel<PREC, false, 9> : dcnv2_fused_ta_kernel<PREC, false, 0>;
       }
       const int grid = p.num_tiles < di->sm_count ? p.num_tiles : di->sm_count;
-      kfn<<<grid, kTaThreads, p.smem_bytes, st>>>(a, tmap);
-      e = cudaGetLastError();
+      cudaLaunchAttribute at[2];
+      const cudaLaunchConfig_t cfg = main_launch_config(grid, kTaThreads, p.smem_bytes, st, at,
+                                                        false);
+      e = cudaLaunchKernelEx(&cfg, kfn, a, tmap);
       mk.mark(st);
       return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
     }
@@ -633,8 +641,8 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
       int clusters = di->pair_clusters[PREC].load(std::memory_order_acquire);
       if (clusters <= 0) {
         // co-resident CTA pairs of this kernel (one CTA per SM); a persistent grid of that size
-        cudaLaunchAttribute qa[1];
-        cudaLaunchConfig_t qc = pair_launch_config(1, p.smem_bytes, st, qa);
+        cudaLaunchAttribute qa[2];
+        cudaLaunchConfig_t qc = main_launch_config(1, kThreads, p.smem_bytes, st, qa, true);
         if (cudaOccupancyMaxActiveClusters(&clusters, kfn, &qc) != cudaSuccess || clusters < 1) {
           cudaGetLastError();
           clusters = di->sm_count / 2;
@@ -642,8 +650,8 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
         di->pair_clusters[PREC].store(clusters, std::memory_order_release);
       }
       const int nc = p.num_tiles < clusters ? p.num_tiles : clusters;
-      cudaLaunchAttribute at[1];
-      cudaLaunchConfig_t cfg = pair_launch_config(2 * nc, p.smem_bytes, st, at);
+      cudaLaunchAttribute at[2];
+      cudaLaunchConfig_t cfg = main_launch_config(2 * nc, kThreads, p.smem_bytes, st, at, true);
       e = cudaLaunchKernelEx(&cfg, kfn, a, tmap);
       mk.mark(st);
       return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
@@ -656,9 +664,11 @@ dcnv2_status launch_fused(const Plan& p, DevInfo* di, int dev, const void* x, co
     if (p.precise)
       kfn = k3 ? dcnv2_fused_kernel<PREC, true, 9, false> : dcnv2_fused_kernel<PREC, true, 0, false>;
   }
-  kfn<<<grid, kThreads, p.smem_bytes, st>>>(a, tmap);
+  cudaLaunchAttribute at[2];
+  const cudaLaunchConfig_t cfg = main_launch_config(grid, kThreads, p.smem_bytes, st, at, false);
+  e = cudaLaunchKernelEx(&cfg, kfn, a, tmap);
   mk.mark(st);
-  return cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
+  return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
 }
 
 dcnv2_status launch_f32_exact(const Plan& p, DevInfo* di, const void* x, const void* offset,

@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const WaitCtx wc{args.timeout_ns, args.err, abort_flag};
+  ptx::griddep_launch_dependents();  // the layer's main kernel may come up on free SMs
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -110,6 +111,9 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the setup above overlaps the tail of the kernel ahead (programmatic dependent launch); its
+  // outputs (the channels-last x, packed weights, cleared error word) are read only from here
+  ptx::griddep_wait();
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer (A box + B tile)

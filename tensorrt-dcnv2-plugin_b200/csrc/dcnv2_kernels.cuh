@@ -474,6 +474,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   else __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the setup above overlaps the tail of the kernel ahead (programmatic dependent launch); its
+  // outputs (the channels-last x, packed weights, cleared error word) are read only from here
+  ptx::griddep_wait();
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer (weights)
@@ -1375,6 +1378,9 @@ struct PrepassArgs {
 template <int PREC>
 __global__ void __launch_bounds__(256) prepass_kernel(const PrepassArgs a) {
   using XT = typename PrecTraits<PREC>::X;
+  // the main kernel (launched with programmatic stream serialization) may come up on SMs this
+  // grid leaves free and run its setup; it waits for this grid's completion before reading
+  ptx::griddep_launch_dependents();
   const int b = static_cast<int>(blockIdx.x);
   if (b < a.tr_blocks) {
     const int bx = b % a.tiles_x, r = b / a.tiles_x;

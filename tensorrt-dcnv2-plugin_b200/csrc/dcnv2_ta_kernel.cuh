@@ -248,6 +248,9 @@ __global__ void __launch_bounds__(kTaThreads, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the setup above overlaps the tail of the kernel ahead (programmatic dependent launch); its
+  // outputs (the channels-last x, packed weights, cleared error word) are read only from here
+  ptx::griddep_wait();
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer (weights)

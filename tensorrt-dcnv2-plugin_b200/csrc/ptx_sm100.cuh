@@ -368,6 +368,17 @@ __device__ __forceinline__ uint32_t cvt_rna_tf32(float v) {
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization may
+// start before the kernel ahead of it in the stream completes; griddep_wait blocks until that
+// kernel has completed and its memory operations are visible (a no-op without the launch
+// attribute). griddep_launch_dependents lets the dependent kernel be scheduled once every block
+// of this one has issued it.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
 }
