@@ -677,25 +677,26 @@ dcnv2_status launch_f32_exact(const Plan& p, DevInfo* di, const void* x, const v
   int* err = reinterpret_cast<int*>(ws);
   float* x_nhwc = reinterpret_cast<float*>(ws + p.off_x);
   float* wplain = reinterpret_cast<float*>(ws + p.off_w);
-  const int HW = p.H * p.W;
-  for (int n0 = 0; n0 < p.N; n0 += 65535) {
-    const int nb = p.N - n0 < 65535 ? p.N - n0 : 65535;
-    dim3 g(static_cast<unsigned>(cdiv(HW, 32)), static_cast<unsigned>(cdiv(p.C, 32)),
-           static_cast<unsigned>(nb));
-    mk.mark(st);
-    nchw_to_nhwc_kernel<float><<<g, 256, 0, st>>>(
-        reinterpret_cast<const float*>(x) + size_t(n0) * p.C * HW, x_nhwc + size_t(n0) * p.C * HW,
-        p.C, HW);
-  }
+  // one pre-pass launch: transpose (32 x 32 tiles) and k-major weight packing
   {
+    const int HW = p.H * p.W;
+    PrepassPlainArgs pa;
+    pa.x = reinterpret_cast<const float*>(x); pa.xt = x_nhwc; pa.C = p.C; pa.HW = HW;
+    pa.tiles_x = static_cast<int>(cdiv(HW, 32));
+    pa.tiles_y = static_cast<int>(cdiv(p.C, 32));
+    const int64_t tr_blocks = int64_t(pa.tiles_x) * pa.tiles_y * p.N;
     const size_t total = size_t(p.x_ctiles) * p.numKB * kXK * kXCo;
-    int64_t blocks = cdiv(static_cast<int64_t>(total), 256);
+    int64_t pk_blocks = cdiv(static_cast<int64_t>(total), 256);
     const int64_t cap = int64_t(di->sm_count) * 8;
-    if (blocks > cap) blocks = cap;
+    if (pk_blocks > cap) pk_blocks = cap;
+    if (pk_blocks < 1) pk_blocks = 1;
+    if (tr_blocks + pk_blocks >= (int64_t(1) << 31)) return DCNV2_ERR_INVALID_ARG;
+    pa.tr_blocks = static_cast<int>(tr_blocks);
+    pa.w = reinterpret_cast<const float*>(weight); pa.wp = wplain; pa.err = err;
+    pa.O = p.O; pa.T = p.T; pa.Cg = p.Cg; pa.CBg = p.CBg; pa.numKB = p.numKB;
+    pa.ctiles = p.x_ctiles;
     mk.mark(st);
-    pack_weights_plain_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(
-        reinterpret_cast<const float*>(weight), wplain, err, p.O, p.C, p.T, p.Cg, p.CBg, p.numKB,
-        p.x_ctiles);
+    prepass_plain_kernel<<<static_cast<unsigned>(tr_blocks + pk_blocks), 256, 0, st>>>(pa);
   }
   ExactArgs a;
   a.x_nhwc = x_nhwc; a.offset = reinterpret_cast<const float*>(offset);
@@ -715,9 +716,12 @@ dcnv2_status launch_f32_exact(const Plan& p, DevInfo* di, const void* x, const v
     di->attr_set.fetch_or(kExactBit, std::memory_order_acq_rel);
   }
   mk.mark(st);
-  dcnv2_f32_exact_kernel<<<static_cast<unsigned>(grid), kXThreads * kXGroups, kXSmemBytes, st>>>(a);
+  cudaLaunchAttribute at[2];
+  const cudaLaunchConfig_t cfg = main_launch_config(static_cast<int>(grid), kXThreads * kXGroups,
+                                                    kXSmemBytes, st, at, false);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, dcnv2_f32_exact_kernel, a);
   mk.mark(st);
-  return cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
+  return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? DCNV2_OK : DCNV2_ERR_CUDA;
 }
 
 template <int PREC>
@@ -807,9 +811,7 @@ int32_t dcnv2_launch_count(const dcnv2_desc* desc) {
   Plan p;
   if (make_plan(desc, &p) != DCNV2_OK) return 0;
   if (p.kind == KIND_SIMT) return 1;
-  if (p.kind == KIND_TCGEN05) return 2;  // pre-pass (transpose + weight packing), main kernel
-  const int64_t zsplits = (p.N + 65534) / 65535;
-  return static_cast<int32_t>(zsplits + 2);
+  return 2;  // pre-pass (transpose + weight packing), main kernel
 }
 
 static dcnv2_status forward_impl(const dcnv2_desc* desc, const void* x, const void* offset,

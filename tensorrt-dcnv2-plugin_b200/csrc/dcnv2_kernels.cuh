@@ -1435,6 +1435,8 @@ struct ExactArgs {
 
 __global__ void __launch_bounds__(kXThreads * kXGroups, 1) dcnv2_f32_exact_kernel(const ExactArgs a) {
   extern __shared__ __align__(16) float xsm[];
+  // launched with programmatic stream serialization: the pre-pass's outputs are read from here
+  ptx::griddep_wait();
   const int grp = threadIdx.x / kXThreads;  // K half
   const int tid = threadIdx.x - grp * kXThreads;
   float (*As)[kXK][kXPx] = reinterpret_cast<float (*)[kXK][kXPx]>(xsm + grp * kXGroupFloats);
@@ -1579,14 +1581,14 @@ __global__ void __launch_bounds__(kXThreads * kXGroups, 1) dcnv2_f32_exact_kerne
 }
 
 // Weights for the fp32-exact kernel: [ctile][kb][k][128 co], zero padded.
-__global__ void __launch_bounds__(256) pack_weights_plain_kernel(const float* __restrict__ w,
-                                                                 float* __restrict__ wp, int* err,
-                                                                 int O, int C, int T, int Cg,
-                                                                 int CBg, int numKB, int ctiles) {
-  if (blockIdx.x == 0 && threadIdx.x == 0) *err = 0;
+__device__ __forceinline__ void pack_weights_plain_body(const float* __restrict__ w,
+                                                        float* __restrict__ wp, int* err, int O,
+                                                        int C, int T, int Cg, int CBg, int numKB,
+                                                        int ctiles, int blk, int nblk) {
+  if (blk == 0 && threadIdx.x == 0) *err = 0;
   const size_t total = static_cast<size_t>(ctiles) * numKB * kXK * kXCo;
-  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+  for (size_t idx = blk * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(nblk) * blockDim.x) {
     const int co = static_cast<int>(idx % kXCo);
     const int k = static_cast<int>((idx / kXCo) % kXK);
     const size_t blk = idx / (static_cast<size_t>(kXCo) * kXK);
@@ -1598,6 +1600,30 @@ __global__ void __launch_bounds__(256) pack_weights_plain_kernel(const float* __
     float v = 0.f;
     if (o < O && cig < Cg) v = w[(static_cast<size_t>(o) * C + g * Cg + cig) * T + t];
     wp[idx] = v;
+  }
+}
+
+// The fp32-exact path's two pre-passes in one launch, as prepass_kernel: blocks [0, tr_blocks)
+// transpose x to channels-last (32 x 32 tiles), the rest pack the weights k-major.
+struct PrepassPlainArgs {
+  const float* x;
+  float* xt;
+  int C, HW, tiles_x, tiles_y, tr_blocks;
+  const float* w;
+  float* wp;
+  int* err;
+  int O, T, Cg, CBg, numKB, ctiles;
+};
+
+__global__ void __launch_bounds__(256) prepass_plain_kernel(const PrepassPlainArgs a) {
+  ptx::griddep_launch_dependents();
+  const int b = static_cast<int>(blockIdx.x);
+  if (b < a.tr_blocks) {
+    const int bx = b % a.tiles_x, r = b / a.tiles_x;
+    transpose_tile<float>(a.x, a.xt, a.C, a.HW, bx, r % a.tiles_y, r / a.tiles_y);
+  } else {
+    pack_weights_plain_body(a.w, a.wp, a.err, a.O, a.C, a.T, a.Cg, a.CBg, a.numKB, a.ctiles,
+                            b - a.tr_blocks, static_cast<int>(gridDim.x) - a.tr_blocks);
   }
 }
 
