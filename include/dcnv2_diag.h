@@ -40,9 +40,10 @@ DCNV2_API const char* dcnv2_diag_main_kernel(const dcnv2_desc* desc);
 /* Kernel selection for measurements and tests, process-wide. kernel: 0 = automatic (A operand in
  * tensor memory for fp16 / int8 layers of at most 256 output channels, in shared memory above),
  * 1 = A in tensor memory for every fp16 / int8 layer (one output-channel chunk of at most 256 per
- * tile), 2 = A in shared memory always. pair: 0 = automatic (CTA pairs, tcgen05 cta_group::2,
- * for fp16 / int8 tiles of the A-in-shared-memory kernel with more than 256 output channels, one
- * CTA per tile otherwise), 1 = CTA pairs for every fp16 / int8 tile, 2 = one CTA per tile always.
+ * tile), 2 = A in shared memory always. pair (A-in-shared-memory kernel only; the TMEM-A kernel
+ * always runs one CTA per tile): 0 = automatic (CTA pairs, tcgen05 cta_group::2, for fp16 / int8
+ * tiles with more than 256 output channels, one CTA per tile otherwise), 1 = CTA pairs for every
+ * fp16 / int8 tile, 2 = one CTA per tile always.
  * The starting values come from the environment, read once per process: DCNV2_KERNEL=ta|smem,
  * DCNV2_PAIR=1|0. Change the selection only between forwards: dcnv2_workspace_size and
  * dcnv2_forward must see the same one. */

@@ -272,8 +272,8 @@ class Kernel(enum.IntEnum):
 
 
 class Pair(enum.IntEnum):
-    """CTA-pair selection of dcnv2_diag_set_kernel_override."""
-    AUTO = 0     # pairs for A-in-shared-memory tiles of more than 256 output channels
+    """CTA-pair selection of dcnv2_diag_set_kernel_override (A-in-shared-memory kernel only)."""
+    AUTO = 0     # pairs for tiles of more than 256 output channels
     PAIRS = 1    # every fp16 / int8 tile on a CTA pair (tcgen05 cta_group::2)
     SINGLE = 2   # one CTA per tile
 
