@@ -66,7 +66,10 @@ typedef enum {
 enum {
   DCNV2_MATH_DEFAULT = 0,    /* fp16: tensor cores, packed-f16 sampler; int8: tensor cores, exact
                                 int32 accumulation; fp32: fused CUDA-core kernel, fp32-exact */
-  DCNV2_MATH_PRECISE = 1,    /* fp16: fp32 sampler arithmetic (one rounding per column value) */
+  DCNV2_MATH_PRECISE = 1,    /* fp16: fp32 sampler arithmetic (one rounding per column value);
+                                int8: each column value is the reference's fp32 sample
+                                m * bilinear(x_q) rounded to nearest and clamped to +-127, on the
+                                one-thread-per-output kernel (a cross-check mode, slow) */
   DCNV2_MATH_TF32 = 2,       /* fp32 only: single-pass TF32 tensor cores (own, looser bound) */
   DCNV2_MATH_SIMT = 3,       /* one thread per output on CUDA cores (any shape; cross-check) */
   DCNV2_MATH_TF32X3 = 4      /* fp32 only: 3xTF32 split on tensor cores (own bound, ~5e-5 rel.) */

@@ -129,7 +129,7 @@ struct Plan {
   bool use_win = false;
   int win_rows = 0, win_top = 0;
   uint32_t win_bytes = 0;
-  bool tf32_single = false, precise = false;
+  bool tf32_single = false, precise = false, i8_rint = false;
   // A operand in TMEM (dcnv2_fused_ta_kernel): A ring in TMEM, B ring in shared memory
   bool ta = false;
   int a_stages = 0, b_stages = 0;
@@ -240,7 +240,7 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
   if (prec < 0) return DCNV2_ERR_UNSUPPORTED;
   if ((d->math == DCNV2_MATH_TF32 || d->math == DCNV2_MATH_TF32X3) && prec != PREC_F32)
     return DCNV2_ERR_INVALID_ARG;
-  if (d->math == DCNV2_MATH_PRECISE && prec != PREC_F16) return DCNV2_ERR_INVALID_ARG;
+  if (d->math == DCNV2_MATH_PRECISE && prec == PREC_F32) return DCNV2_ERR_INVALID_ARG;
   const int64_t ho = (int64_t(d->h) + 2 * int64_t(d->padding) -
                       int64_t(d->dilation) * (d->kernel - 1) - 1);
   const int64_t wo = (int64_t(d->w) + 2 * int64_t(d->padding) -
@@ -263,13 +263,15 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
     return DCNV2_ERR_INVALID_ARG;
   p.P = static_cast<int>(P);
   p.tf32_single = (d->math == DCNV2_MATH_TF32);
-  p.precise = (d->math == DCNV2_MATH_PRECISE);
+  p.precise = (d->math == DCNV2_MATH_PRECISE) && prec == PREC_F16;
 
   const bool cg_ok = p.Cg % chunk_elems_of(prec) == 0;
   // fp32 defaults to the fp32-exact CUDA-core fused kernel; the tensor-core kinds of fp32 are
   // opt-in (TF32, TF32X3) because their accumulation error exceeds fp32 rounding.
   const bool f32_exact = prec == PREC_F32 && d->math == DCNV2_MATH_DEFAULT && cg_ok;
-  p.fused = (d->math != DCNV2_MATH_SIMT) && cg_ok && !f32_exact;
+  // int8 with DCNV2_MATH_PRECISE: the reference-rounding column rule on the per-output kernel
+  p.i8_rint = prec == PREC_I8 && d->math == DCNV2_MATH_PRECISE;
+  p.fused = (d->math != DCNV2_MATH_SIMT) && cg_ok && !f32_exact && !p.i8_rint;
   if (f32_exact) {
     p.kind = KIND_F32_EXACT;
     p.CBg = static_cast<int>(cdiv(p.Cg, kXK));
@@ -733,7 +735,7 @@ dcnv2_status launch_simt(const Plan& p, DevInfo* di, const void* x, const void* 
   a.x = x; a.offset = offset; a.mask = mask; a.w = weight; a.bias = bias; a.y = y;
   a.N = p.N; a.C = p.C; a.H = p.H; a.W = p.W; a.O = p.O; a.Ho = p.Ho; a.Wo = p.Wo; a.P = p.P;
   a.K = p.K; a.T = p.T; a.stride = p.stride; a.pad = p.pad; a.dil = p.dil; a.dg = p.dg;
-  a.Cg = p.Cg; a.scale = scale;
+  a.Cg = p.Cg; a.scale = scale; a.i8_rint = p.i8_rint ? 1 : 0;
   const size_t total = size_t(p.N) * p.O * p.P;
   int64_t blocks = cdiv(static_cast<int64_t>(total), 256);
   const int64_t cap = int64_t(di->sm_count) * 16;

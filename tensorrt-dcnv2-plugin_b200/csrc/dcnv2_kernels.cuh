@@ -1636,6 +1636,7 @@ struct SimtArgs {
   const void* x; const void* offset; const void* mask; const void* w; const void* bias; void* y;
   int N, C, H, W, O, Ho, Wo, P, K, T, stride, pad, dil, dg, Cg;
   float scale;
+  int i8_rint;  // int8: column = clamp(rint(m * bilinear(x_q)), -127, 127) in fp32 (see below)
 };
 
 template <int PREC>
@@ -1662,19 +1663,22 @@ __global__ void __launch_bounds__(256) dcnv2_simt_kernel(const SimtArgs a) {
         const size_t gmsk = (static_cast<size_t>(n) * a.dg + g) * a.T + t;
         const float dh = load_geom_value(offp + goff * a.P + p);
         const float dw = load_geom_value(offp + (goff + 1) * a.P + p);
-        float m = load_geom_value(maskp + gmsk * a.P + p);
-        if (PREC == PREC_I8) m = i8_mask(m);
+        const float m_raw = load_geom_value(maskp + gmsk * a.P + p);
+        const float m = PREC == PREC_I8 ? i8_mask(m_raw) : m_raw;
         const float hf = __fadd_rn(static_cast<float>(oh * a.stride - a.pad + ki * a.dil), dh);
         const float wf = __fadd_rn(static_cast<float>(ow * a.stride - a.pad + kj * a.dil), dw);
         const bool inside = !(hf <= -1.f || hf >= static_cast<float>(a.H) || wf <= -1.f ||
                               wf >= static_cast<float>(a.W));
         float wt[4] = {0.f, 0.f, 0.f, 0.f};
+        float area[4] = {0.f, 0.f, 0.f, 0.f};  // corner areas without the mask (int8 rint rule)
         int idx4[4] = {-1, -1, -1, -1};
         if (inside) {
           const float h0f = floorf(hf), w0f = floorf(wf);
           const int h0 = static_cast<int>(h0f), w0 = static_cast<int>(w0f);
           const float lh = __fsub_rn(hf, h0f), lw = __fsub_rn(wf, w0f);
           const float hh = __fsub_rn(1.f, lh), hw = __fsub_rn(1.f, lw);
+          area[0] = __fmul_rn(hh, hw); area[1] = __fmul_rn(hh, lw);
+          area[2] = __fmul_rn(lh, hw); area[3] = __fmul_rn(lh, lw);
           if (h0 >= 0 && w0 >= 0) { wt[0] = __fmul_rn(m, __fmul_rn(hh, hw)); idx4[0] = h0 * a.W + w0; }
           if (h0 >= 0 && w0 + 1 <= a.W - 1) { wt[1] = __fmul_rn(m, __fmul_rn(hh, lw)); idx4[1] = h0 * a.W + w0 + 1; }
           if (h0 + 1 <= a.H - 1 && w0 >= 0) { wt[2] = __fmul_rn(m, __fmul_rn(lh, hw)); idx4[2] = (h0 + 1) * a.W + w0; }
@@ -1700,11 +1704,25 @@ __global__ void __launch_bounds__(256) dcnv2_simt_kernel(const SimtArgs a) {
           v = __fmaf_rn(wt[3], xv[3], v);
           const size_t widx = (static_cast<size_t>(o) * a.C + c) * a.T + t;
           if (PREC == PREC_I8) {
-            int sum = 32768;  // fixed-point column value (rule at i8_mix_fx)
+            int q;
+            if (a.i8_rint) {
+              // The reference's fp32 column m * bilinear(x_q) (src/dcn_kernel.cu:19-30, :234),
+              // every product and sum rounded as written (corner area * value, left to right,
+              // then times the unclamped mask), rounded to nearest even and clamped to +-127.
+              float b = __fmul_rn(area[0], xv[0]);
+              b = __fadd_rn(b, __fmul_rn(area[1], xv[1]));
+              b = __fadd_rn(b, __fmul_rn(area[2], xv[2]));
+              b = __fadd_rn(b, __fmul_rn(area[3], xv[3]));
+              const float cv = __fmul_rn(m_raw, b);
+              q = __float2int_rn(cv);  // NaN -> 0
+              q = q < -127 ? -127 : (q > 127 ? 127 : q);
+            } else {
+              int sum = 32768;  // fixed-point column value (rule at i8_mix_fx)
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              sum += static_cast<int>(i8_weight(wt[k])) * static_cast<int>(xv[k]);
-            const int q = sum >> 16;
+              for (int k = 0; k < 4; ++k)
+                sum += static_cast<int>(i8_weight(wt[k])) * static_cast<int>(xv[k]);
+              q = sum >> 16;
+            }
             iacc += static_cast<long long>(q) * reinterpret_cast<const int8_t*>(a.w)[widx];
           } else if (PREC == PREC_F16) {
             const float cv = __half2float(__float2half_rn(v));

@@ -251,3 +251,12 @@ def test_binary_arch_without_device():
         pytest.skip("a GPU is present (the GPU test covers the query)")
     v = ctypes.c_int32(0)
     assert capi.lib.dcnv2_diag_binary_arch(ctypes.byref(v)) == Status.ERR_NO_DEVICE
+
+
+def test_int8_precise_takes_the_reference_rounding_kernel():
+    """int8 with DCNV2_MATH_PRECISE computes each column as the reference's fp32 sample rounded
+    to nearest, on the one-thread-per-output kernel; fp32 has no PRECISE mode."""
+    d = capi.make_desc(2, 64, 16, 16, 32, dtype=DType.INT8, math=Math.PRECISE)
+    assert capi.uses_tensor_cores(d) == 0
+    assert capi.main_kernel(d) == "dcnv2_simt_kernel"
+    assert capi.uses_tensor_cores(capi.make_desc(2, 64, 16, 16, 32, dtype=DType.INT8)) == 1

@@ -129,6 +129,24 @@ def test_int8_golden(name):
     check_int8(fx, y, xq, xs, wq, ws)
 
 
+@pytest.mark.parametrize("name", ["kat_16c_32.npz", "tv_oob.npz", "tv_n2_dg2_s2.npz",
+                                  "tv_d2_p2_dg8.npz"])
+def test_int8_precise_is_the_reference_rounding_rule(name):
+    """int8 with DCNV2_MATH_PRECISE: each column is clamp(rint(m * bilinear(x_q)), -127, 127)
+    in the reference's fp32 order (src/dcn_kernel.cu:19-30, :234) — the oracle's "rint" rule —
+    so the integer accumulators match it exactly (|y - y_exact| <= 1e-6 * (|acc * s| + |b|))."""
+    fx = load(name)
+    xq, xs, wq, ws = quantized(fx)
+    y = run_int8(fx, xq, xs, wq, ws, Math.PRECISE)
+    n, o, ho, wo = y.shape
+    yx, acc = oracle.forward_i8_exact_band(xq, fx["offset"], fx["mask"], wq, fx["bias"], xs, ws,
+                                           0, ho * wo, *oattrs(fx), rule="rint")
+    s = float(np.float32(xs) * np.float32(ws))
+    denom = np.abs(acc.astype(np.float64) * s) + np.abs(fx["bias"]).reshape(1, -1, 1)
+    err = np.abs(y.reshape(n, o, -1).astype(np.float64) - yx)
+    assert np.all(err <= INT8_REL * denom + 1e-30), float((err / (denom + 1e-30)).max())
+
+
 @pytest.mark.parametrize("name", ["kat_16c_32.npz", "tv_n2_dg2_s2.npz", "tv_odd.npz"])
 def test_simt_path_matches(name):
     fx = load(name)
