@@ -314,7 +314,8 @@ dcnv2_status make_plan(const dcnv2_desc* d, Plan* pl) {
     p.b_kb_bytes = size_t(nB) * p.nrows * kRowBytes;
     p.b_stage_bytes = static_cast<uint32_t>(p.b_kb_bytes / (p.pair ? 2 : 1));
     const size_t per_stage = p.a_stage_bytes + p.b_stage_bytes;
-    const size_t fixed = 1024 + 512;  // alignment slack + barriers and flags
+    // alignment slack + barriers and flags + the staged bias of one output-channel chunk
+    const size_t fixed = 1024 + 512 + size_t(p.nrows) * sizeof(float);
     int stages = static_cast<int>((kSmemLimit - fixed) / per_stage);
     if (stages > kMaxStages) stages = kMaxStages;
     const int64_t cta_tiles_per_img = cdiv(P, kTileM);

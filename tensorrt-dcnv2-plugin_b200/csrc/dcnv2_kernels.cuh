@@ -400,6 +400,73 @@ __device__ __noinline__ void mma_issuer(const MmaParams mp) {
   wait_bar(mp.drain, 0, wc, DCNV2_DEVERR_TIMEOUT_DRAIN);
 }
 
+// ------------------------------------------------------------------ epilogue block
+// 16 accumulator columns (output channels o_chunk + col ...) of one pixel per lane (pixel p,
+// odd = p & 1 within the lane pair): + bias (int8: fma(float(acc), x_scale*w_scale, bias)), one
+// rounding to the output type, stores of y (yimg = y of the tile's image). Bias comes from the
+// fp32 copy in shared memory when `staged` (a global load per column would wait for L2 on every
+// block: little L1 is left beside the shared memory these kernels use). When `paired` (P even,
+// y aligned to two elements), lanes 2j and 2j+1 swap one value per channel pair so that each
+// store covers the pixel pair (p - odd, p - odd + 1): the even lane stores the even channel, the
+// odd lane the odd one. Layer sizes are read from the kernel arguments (not copied per tile:
+// the kernels that call this have no registers to spare).
+template <int PREC>
+__device__ __forceinline__ void epilogue_block(const FusedArgs& args, const float* bias_smem,
+                                               bool staged, bool paired,
+                                               typename PrecTraits<PREC>::Y* yimg, int o_chunk,
+                                               int p, int odd, const uint32_t (&r)[16], int col) {
+  using YT = typename PrecTraits<PREC>::Y;
+  const int o0 = o_chunk + col;
+  const int pe = p - odd;
+  float bo[16];
+  if (staged) {
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      const float4 b4 = *reinterpret_cast<const float4*>(bias_smem + col + i);
+      bo[i] = b4.x; bo[i + 1] = b4.y; bo[i + 2] = b4.z; bo[i + 3] = b4.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int o = o0 + i < args.O ? o0 + i : args.O - 1;
+      bo[i] = !args.bias ? 0.f
+              : PREC == PREC_F16 ? __half2float(reinterpret_cast<const __half*>(args.bias)[o])
+                                 : __ldg(reinterpret_cast<const float*>(args.bias) + o);
+    }
+  }
+  float v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    if (PREC == PREC_I8) v[i] = __fmaf_rn(__int2float_rn(static_cast<int>(r[i])), args.scale, bo[i]);
+    else v[i] = __uint_as_float(r[i]) + bo[i];
+  }
+  if (paired) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float keep = odd ? v[2 * i + 1] : v[2 * i];
+      const float send = odd ? v[2 * i] : v[2 * i + 1];
+      const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+      const float lo = odd ? recv : keep, hi = odd ? keep : recv;
+      const int o = o0 + 2 * i + odd;
+      if (o < args.O && pe < args.P) {
+        YT* dst = yimg + static_cast<size_t>(o) * args.P + pe;
+        if (PREC == PREC_F16) *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(lo, hi);
+        else *reinterpret_cast<float2*>(dst) = make_float2(lo, hi);
+      }
+    }
+  } else if (p < args.P) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int o = o0 + i;
+      if (o < args.O) {
+        YT* dst = yimg + static_cast<size_t>(o) * args.P + p;
+        if (PREC == PREC_F16) *reinterpret_cast<__half*>(dst) = __float2half_rn(v[i]);
+        else *reinterpret_cast<float*>(dst) = v[i];
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ the fused kernel
 // PAIR: launched as clusters of two CTAs that share each tile of 256 pixels (cta_group::2).
 // Rank 0 (the leader) issues M = 256 MMAs reading rows 0-127 of A and B rows [0, N/2) from its own
@@ -433,6 +500,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t win_empty = win_full + 16;              // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * S + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // bias of the (single) output-channel chunk as fp32, after the 512 bytes of barriers
+  float* bias_smem = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 512);
   const WaitCtx wc{args.timeout_ns, args.err, abort_flag};
   // Tile schedule: CTAs (pairs) stride over the tiles. pix_base(pt) is the first pixel of this
   // CTA's 128 rows in tile pt.
@@ -459,6 +528,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     *abort_flag = 0;
     ptx::fence_mbar_init();
+  }
+  if (args.cchunks == 1) {
+    for (int i = threadIdx.x; i < args.nrows; i += blockDim.x) {
+      float bv = 0.f;
+      if (args.bias && i < args.O)
+        bv = PREC == PREC_F16 ? __half2float(reinterpret_cast<const __half*>(args.bias)[i])
+                              : reinterpret_cast<const float*>(args.bias)[i];
+      bias_smem[i] = bv;
+    }
   }
   if (warp == kMmaWarp) {
     if (PAIR) {
@@ -558,8 +636,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < kSampWarp0) {
     // ------------------------------------------------------------ epilogue
+    // Per 16 accumulator columns: tcgen05.ld (the next block's load overlaps this block's
+    // stores), then epilogue_block (+ bias from shared memory, convert, paired stores). With
+    // 512 output channels the accumulator fills the TMEM, so the next tile's MMAs wait for this
+    // drain: its speed is on the critical path.
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const uint32_t acc_cols = static_cast<uint32_t>(args.nrows);
+    const bool paired = (args.P % 2) == 0 &&
+                        (reinterpret_cast<uintptr_t>(args.y) % (2 * sizeof(YT))) == 0;
+    const bool staged = args.cchunks == 1;
+    const int odd = lane & 1;
     int tl = 0;
     for (int tile = tile0; tile < args.num_tiles; tile += tstep, ++tl) {
       const int acc = tl % args.acc_bufs;
@@ -572,39 +658,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       int img, pt, cc;
       decode_tile(args, tile, img, pt, cc);
       const int p = pix_base(pt) + q * 32 + lane;
-      const bool pvalid = p < args.P;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * acc_cols;
       const int o_chunk = cc * args.nrows;
       YT* yimg = reinterpret_cast<YT*>(args.y) + static_cast<size_t>(img) * args.O * args.P;
-      for (int col = 0; col < args.nrows; col += 16) {
-        const int o0 = o_chunk + col;
-        if (o0 >= args.O) break;  // warp-uniform
-        uint32_t r[16];
-        ptx::tmem_ld_32x32b_x16(taddr + col, r);
-        ptx::tmem_wait_ld();
-        if (pvalid) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int o = o0 + i;
-            if (o < args.O) {
-              YT* dst = yimg + static_cast<size_t>(o) * args.P + p;
-              if (PREC == PREC_F16) {
-                const float bo = args.bias
-                                     ? __half2float(reinterpret_cast<const __half*>(args.bias)[o])
-                                     : 0.f;
-                *reinterpret_cast<__half*>(dst) = __float2half_rn(__uint_as_float(r[i]) + bo);
-              } else if (PREC == PREC_I8) {
-                const float bo = args.bias ? __ldg(reinterpret_cast<const float*>(args.bias) + o)
-                                           : 0.f;
-                const float accf = __int2float_rn(static_cast<int>(r[i]));
-                *reinterpret_cast<float*>(dst) = __fmaf_rn(accf, args.scale, bo);
-              } else {
-                const float bo = args.bias ? __ldg(reinterpret_cast<const float*>(args.bias) + o)
-                                           : 0.f;
-                *reinterpret_cast<float*>(dst) = __uint_as_float(r[i]) + bo;
-              }
-            }
-          }
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * acc_cols;
+      const int ncols = args.O - o_chunk < args.nrows ? args.O - o_chunk : args.nrows;
+      uint32_t ra[16], rb[16];
+      ptx::tmem_ld_32x32b_x16(taddr, ra);
+      for (int col = 0; col < ncols; col += 32) {  // warp-uniform bounds
+        ptx::tmem_wait_ld_regs(ra);
+        if (col + 16 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 16, rb);
+        epilogue_block<PREC>(args, bias_smem, staged, paired, yimg, o_chunk, p, odd, ra, col);
+        if (col + 16 < ncols) {
+          ptx::tmem_wait_ld_regs(rb);
+          if (col + 32 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 32, ra);
+          epilogue_block<PREC>(args, bias_smem, staged, paired, yimg, o_chunk, p, odd, rb,
+                               col + 16);
         }
       }
       ptx::tc_fence_before();

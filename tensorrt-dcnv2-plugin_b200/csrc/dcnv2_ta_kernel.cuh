@@ -300,10 +300,8 @@ __global__ void __launch_bounds__(kTaThreads, 1)
   } else if (warp < kSampWarp0) {
     // ------------------------------------------------------------ epilogue
     // Per 16 accumulator columns: tcgen05.ld (the next block's load overlaps this block's
-    // stores), + bias from shared memory (staged at kernel start; a global load per column
-    // would wait for L2 on every block, since the L1 left beside 225 KB of shared memory is
-    // small), convert, store. Lanes 2i and 2i+1 swap one value per channel pair so that each
-    // store covers two pixels, when every pixel pair starts on an aligned address.
+    // stores), + bias from shared memory (staged at kernel start), convert, store: int8 through
+    // epilogue_block; fp16 parks the converted tile in TMEM first (below).
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const bool paired = (args.P % 2) == 0 &&
                         (reinterpret_cast<uintptr_t>(args.y) % (2 * sizeof(YT))) == 0;
@@ -323,58 +321,6 @@ __global__ void __launch_bounds__(kTaThreads, 1)
       const int o_chunk = cc * args.n_mma;
       const int ncols = args.O - o_chunk < args.n_mma ? args.O - o_chunk : args.n_mma;
       YT* yimg = reinterpret_cast<YT*>(args.y) + static_cast<size_t>(img) * args.O * args.P;
-      auto block = [&](const uint32_t (&r)[16], int col) {
-        const int o0 = o_chunk + col;
-        float bo[16];
-        if (staged) {
-#pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            const float4 b4 = *reinterpret_cast<const float4*>(bias_smem + col + i);
-            bo[i] = b4.x; bo[i + 1] = b4.y; bo[i + 2] = b4.z; bo[i + 3] = b4.w;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int o = o0 + i < args.O ? o0 + i : args.O - 1;
-            bo[i] = !args.bias ? 0.f
-                    : PREC == PREC_F16 ? __half2float(reinterpret_cast<const __half*>(args.bias)[o])
-                                       : __ldg(reinterpret_cast<const float*>(args.bias) + o);
-          }
-        }
-        float v[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          if (PREC == PREC_F16) v[i] = __uint_as_float(r[i]) + bo[i];
-          else v[i] = __fmaf_rn(__int2float_rn(static_cast<int>(r[i])), args.scale, bo[i]);
-        }
-        if (paired) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            // lane pair (2j, 2j+1): the even lane stores channel o0+2i, the odd one o0+2i+1,
-            // both for pixels (pe, pe + 1)
-            const float keep = odd ? v[2 * i + 1] : v[2 * i];
-            const float send = odd ? v[2 * i] : v[2 * i + 1];
-            const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
-            const float lo = odd ? recv : keep, hi = odd ? keep : recv;
-            const int o = o0 + 2 * i + odd;
-            if (o < args.O && pe < args.P) {
-              YT* dst = yimg + static_cast<size_t>(o) * args.P + pe;
-              if (PREC == PREC_F16) *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(lo, hi);
-              else *reinterpret_cast<float2*>(dst) = make_float2(lo, hi);
-            }
-          }
-        } else if (p < args.P) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int o = o0 + i;
-            if (o < args.O) {
-              YT* dst = yimg + static_cast<size_t>(o) * args.P + p;
-              if (PREC == PREC_F16) *reinterpret_cast<__half*>(dst) = __float2half_rn(v[i]);
-              else *reinterpret_cast<float*>(dst) = v[i];
-            }
-          }
-        }
-      };
       auto release = [&]() {
         ptx::tc_fence_before();
         __syncwarp();
@@ -456,11 +402,12 @@ __global__ void __launch_bounds__(kTaThreads, 1)
         for (int col = 0; col < ncols; col += 32) {  // warp-uniform bounds
           ptx::tmem_wait_ld_regs(ra);
           if (col + 16 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 16, rb);
-          block(ra, col);
+          epilogue_block<PREC>(args, bias_smem, staged, paired, yimg, o_chunk, p, odd, ra, col);
           if (col + 16 < ncols) {
             ptx::tmem_wait_ld_regs(rb);
             if (col + 32 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 32, ra);
-            block(rb, col + 16);
+            epilogue_block<PREC>(args, bias_smem, staged, paired, yimg, o_chunk, p, odd, rb,
+                                 col + 16);
           }
         }
         release();
