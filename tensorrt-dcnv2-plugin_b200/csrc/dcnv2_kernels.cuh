@@ -95,6 +95,9 @@ struct FusedArgs {
   int tap_pairs;           // int8, 64-channel groups: K-block = taps (2i, 2i+1) x 64 channels
   int precise;             // fp16: fp32 sampler arithmetic
   int tf32_single;         // fp32: hi*hi only (plain TF32)
+  uint32_t epi_off;        // A-in-shared-memory kernel, fp32 output: byte offset of the
+                           // epilogue's TMA-store staging boxes from the barrier block (0: direct
+                           // stores of y)
   unsigned long long timeout_ns;
 };
 
@@ -467,6 +470,47 @@ __device__ __forceinline__ void epilogue_block(const FusedArgs& args, const floa
   }
 }
 
+// Same arithmetic as epilogue_block, written into a staging box of the epilogue's TMA store
+// instead of y: box = [16 channels][32 pixels] of the output type at shared address `box`, lane
+// = pixel (each channel row is 32 consecutive elements, so the lanes' stores are conflict-free).
+template <int PREC>
+__device__ __forceinline__ void epilogue_block_box(const FusedArgs& args, const float* bias_smem,
+                                                   bool staged, int o_chunk,
+                                                   const uint32_t (&r)[16], int col, uint32_t box,
+                                                   int lane) {
+  using YT = typename PrecTraits<PREC>::Y;
+  const int o0 = o_chunk + col;
+  float bo[16];
+  if (staged) {
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      const float4 b4 = *reinterpret_cast<const float4*>(bias_smem + col + i);
+      bo[i] = b4.x; bo[i + 1] = b4.y; bo[i + 2] = b4.z; bo[i + 3] = b4.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int o = o0 + i < args.O ? o0 + i : args.O - 1;
+      bo[i] = !args.bias ? 0.f
+              : PREC == PREC_F16 ? __half2float(reinterpret_cast<const __half*>(args.bias)[o])
+                                 : __ldg(reinterpret_cast<const float*>(args.bias) + o);
+    }
+  }
+  const uint32_t at = box + static_cast<uint32_t>(lane) * sizeof(YT);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t row = at + static_cast<uint32_t>(i) * 32u * sizeof(YT);
+    if (PREC == PREC_F16) {
+      ptx::st_shared_u16(row, __half_as_ushort(__float2half_rn(__uint_as_float(r[i]) + bo[i])));
+    } else if (PREC == PREC_I8) {
+      ptx::st_shared_u32(row, __float_as_uint(
+          __fmaf_rn(__int2float_rn(static_cast<int>(r[i])), args.scale, bo[i])));
+    } else {
+      ptx::st_shared_u32(row, __float_as_uint(__uint_as_float(r[i]) + bo[i]));
+    }
+  }
+}
+
 // ------------------------------------------------------------------ the fused kernel
 // PAIR: launched as clusters of two CTAs that share each tile of 256 pixels (cta_group::2).
 // Rank 0 (the leader) issues M = 256 MMAs reading rows 0-127 of A and B rows [0, N/2) from its own
@@ -476,7 +520,8 @@ __device__ __forceinline__ void epilogue_block(const FusedArgs& args, const floa
 // the barriers of both CTAs.
 template <int PREC, bool PRECISE, int KT, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
-    dcnv2_fused_kernel(const FusedArgs args, const __grid_constant__ CUtensorMap tmap_x) {
+    dcnv2_fused_kernel(const FusedArgs args, const __grid_constant__ CUtensorMap tmap_x,
+                       const __grid_constant__ CUtensorMap tmap_y) {
   using TR = PrecTraits<PREC>;
   using GT = typename TR::G;
   using YT = typename TR::Y;
@@ -646,6 +691,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         (reinterpret_cast<uintptr_t>(args.y) % (2 * sizeof(YT))) == 0;
     const bool staged = args.cchunks == 1;
     const int odd = lane & 1;
+    // TMA-store path (fp32 outputs): two staging boxes per epilogue warp after the staged bias
+    constexpr uint32_t kEpiBoxBytes = 16u * 32u * sizeof(YT);
+    const bool y_tma = PREC != PREC_F16 && args.epi_off != 0;
+    const uint32_t epi_slots = ptx::smem_addr(reinterpret_cast<uint8_t*>(bars) + args.epi_off);
+    int nbox = 0;
     int tl = 0;
     for (int tile = tile0; tile < args.num_tiles; tile += tstep, ++tl) {
       const int acc = tl % args.acc_bufs;
@@ -663,16 +713,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * acc_cols;
       const int ncols = args.O - o_chunk < args.nrows ? args.O - o_chunk : args.nrows;
       uint32_t ra[16], rb[16];
-      ptx::tmem_ld_32x32b_x16(taddr, ra);
-      for (int col = 0; col < ncols; col += 32) {  // warp-uniform bounds
-        ptx::tmem_wait_ld_regs(ra);
-        if (col + 16 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 16, rb);
-        epilogue_block<PREC>(args, bias_smem, staged, paired, yimg, o_chunk, p, odd, ra, col);
-        if (col + 16 < ncols) {
-          ptx::tmem_wait_ld_regs(rb);
-          if (col + 32 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 32, ra);
-          epilogue_block<PREC>(args, bias_smem, staged, paired, yimg, o_chunk, p, odd, rb,
-                               col + 16);
+      if (y_tma) {
+        // Per 16 columns: the converted [16 channels][32 pixels] box of this warp into one of
+        // its two staging slots, then one TMA store by lane 0 (the parts past P or O are not
+        // written). A slot is rewritten once the store issued from it two boxes earlier has
+        // read it. TMEM is released after the last tcgen05.ld, without waiting for the stores.
+        const int x0 = p - lane;  // first pixel of this warp's 32
+        auto box = [&](const uint32_t (&r)[16], int col) {
+          if (lane == 0) ptx::bulk_wait_group_read<1>();
+          __syncwarp();
+          const uint32_t slot = epi_slots + static_cast<uint32_t>(2 * q + nbox) * kEpiBoxBytes;
+          epilogue_block_box<PREC>(args, bias_smem, staged, o_chunk, r, col, slot, lane);
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && x0 < args.P) {  // a warp wholly past the last pixel stores nothing
+            ptx::tma_store_3d(&tmap_y, slot, x0, o_chunk + col, img);
+            ptx::bulk_commit_group();
+          }
+          nbox ^= 1;
+        };
+        ptx::tmem_ld_32x32b_x16(taddr, ra);
+        for (int col = 0; col < ncols; col += 32) {  // warp-uniform bounds
+          ptx::tmem_wait_ld_regs(ra);
+          if (col + 16 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 16, rb);
+          box(ra, col);
+          if (col + 16 < ncols) {
+            ptx::tmem_wait_ld_regs(rb);
+            if (col + 32 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 32, ra);
+            box(rb, col + 16);
+          }
+        }
+      } else {
+        ptx::tmem_ld_32x32b_x16(taddr, ra);
+        for (int col = 0; col < ncols; col += 32) {  // warp-uniform bounds
+          ptx::tmem_wait_ld_regs(ra);
+          if (col + 16 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 16, rb);
+          epilogue_block<PREC>(args, bias_smem, staged, paired, yimg, o_chunk, p, odd, ra, col);
+          if (col + 16 < ncols) {
+            ptx::tmem_wait_ld_regs(rb);
+            if (col + 32 < ncols) ptx::tmem_ld_32x32b_x16(taddr + col + 32, ra);
+            epilogue_block<PREC>(args, bias_smem, staged, paired, yimg, o_chunk, p, odd, rb,
+                                 col + 16);
+          }
         }
       }
       ptx::tc_fence_before();
@@ -682,6 +764,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         else ptx::mbar_arrive(tempty + 8 * acc);
       }
     }
+    // the TMA stores of y have been performed (and have read their boxes) before the CTA exits
+    if (y_tma && lane == 0) ptx::bulk_wait_group<0>();
+    __syncwarp();
   } else {
     // ------------------------------------------------------------ samplers
     // K order is (group g, channel block cbg, tap t). Thread (pixel slot ps, chunk j) fills rows

@@ -152,6 +152,31 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int 
       : "memory");
 }
 
+// 3-D tiled TMA store of one box from CTA-local shared memory at `src` to `tmap`'s tensor at
+// coordinates {c0, c1, c2} (innermost first; none negative, c0 * element size a multiple of 16
+// bytes); parts of the box outside the tensor are not written. Tracked by this thread's bulk
+// async-groups (bulk_commit_group / bulk_wait_group*).
+__device__ __forceinline__ void tma_store_3d(const void* tmap, uint32_t src, int c0, int c1,
+                                             int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(tmap),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until at most N of this thread's bulk groups still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Waits until at most N of this thread's bulk groups are incomplete (writes performed).
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Makes this thread's generic-proxy shared-memory writes visible to the async proxy
 // (the tensor core reading operands through a matrix descriptor).
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -398,6 +423,12 @@ __device__ __forceinline__ uint32_t ld_shared_u32_volatile(uint32_t addr) {
 }
 // Shared-memory store by 32-bit shared address (volatile: stays before the proxy fence and the
 // mbarrier arrive that publish it).
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, unsigned short v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
+__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
                "r"(v.z), "r"(v.w));
