@@ -8,7 +8,8 @@
 //
 // Built only when TensorRT headers are available (Makefile: TRT_INCLUDE_DIR=/path/to/include),
 // into the same libdcnv2.so; loading the library with dlopen / ctypes.CDLL registers the creator
-// (REGISTER_TENSORRT_PLUGIN), exactly as the reference's libdcnv2.so did.
+// (REGISTER_TENSORRT_PLUGIN), exactly as the reference's libdcnv2.so did, and the library also
+// exports getCreators / setLoggerFinder for IPluginRegistry::loadLibrary.
 
 #include <NvInfer.h>
 #include <NvInferRuntime.h>
@@ -206,3 +207,19 @@ class Creator final : public IPluginCreatorV3One {
 }  // namespace dcnv2_trt
 
 REGISTER_TENSORRT_PLUGIN(dcnv2_trt::Creator);
+
+// Plugin-library entry points of TensorRT 10 (IPluginRegistry::loadLibrary, trtexec
+// --dynamicPlugins): the library's creators, and the logger finder TensorRT hands over before
+// asking for them (this library logs nothing itself, so it is only accepted).
+extern "C" {
+__attribute__((visibility("default"))) void setLoggerFinder(nvinfer1::ILoggerFinder* finder) {
+  (void)finder;
+}
+__attribute__((visibility("default"))) nvinfer1::IPluginCreatorInterface* const* getCreators(
+    int32_t& nbCreators) {
+  static dcnv2_trt::Creator creator;
+  static nvinfer1::IPluginCreatorInterface* const creators[] = {&creator};
+  nbCreators = 1;
+  return creators;
+}
+}
