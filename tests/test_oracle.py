@@ -186,7 +186,7 @@ def test_band_matches_full(golden_dir):
 
 def test_int8_column_rules_agree_on_the_int8_workload():
     """The kernels' int8 column rule (16-bit fixed-point corner weights, integer rounding) against
-    the survey's definition clamp(rint(m * bilinear(x_q)), -127, 127) in the reference's fp32
+    the reference-rounding definition clamp(rint(m * bilinear(x_q)), -127, 127) in the reference's fp32
     arithmetic (src/dcn_kernel.cu:218-235), on one image of the benchmarked int8 workload
     (256 -> 256, 64x64, offsets N(0, 0.5^2) with 5 % at +-70, mask sigmoid(N(0, 1))).
     Measured: 0.017 % of the 9.4 M column values differ, each by 1; mean relative error against
